@@ -1,0 +1,430 @@
+"""Benchmark of the B200 GDN state codec hot path.
+
+One step = one pass of the codec over one batch: int8 quantize (fused
+smoothing) of every head of the workload, then dequantize of every head
+(30 GDN layers x 64 request slots x fp32 state
+[32, 128, 128] = 61,440 heads, ~4 GB fp32 + 1.07 GB codes, contiguous
+slot-major cache, capsule layout).  Under torchrun each rank owns its own 64
+slots (weak scaling, no data-path collective); rank r's slots are global slots
+64r..64r+63 of the seeded synthetic generator.
+
+Output: one JSON line on rank 0 with the device-timed value (inputs resident
+in HBM), an end-to-end value through the public API with host buffers (H2D of
+the states and D2H of the reconstruction inside the timed region), the
+roofline of the dominant kernel, the CPU baseline, clocks sampled during the
+timed region and the launch count.  ``--impl reference`` times the CPU
+restatement of the reference codec (oracle/) on all host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gdn-state-codec_b200"))
+
+METRIC = "codec HBM GB/s (% of B200 peak) and states/sec at 1/2/4/8 B200"
+UNIT = "states/s"
+SLOTS, LAYERS, HEADS = 64, 30, 32
+BYTES_PER_HEAD = {  # algorithmic bytes per head (one launch of each kernel)
+    "quantize": 65536 + 16384 + 512 + 512,
+    "dequantize": 16384 + 512 + 512 + 65536,
+    "projection": 16384 + 512 + 512 + 256 + 512,
+}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--layout", choices=["capsule", "provider"], default="capsule")
+    parser.add_argument("--slots", type=int, default=SLOTS,
+                        help="request slots per GPU (default: config 2's 64)")
+    parser.add_argument("--profile", action="store_true",
+                        help="device-resident steps only (for ncu captures of a small case)")
+    return parser.parse_args()
+
+
+def measured_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm, sm_max, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(sm_max) if sm_max else None,
+            "power_w_max": max(power) if power else None,
+            "samples": len(sm),
+            "reasons": sorted(reasons),
+        }
+
+
+def cpu_baseline(layout: str, target_seconds: float = 3.0) -> dict:
+    """The oracle (C restatement of the reference's quant-only codec,
+    capsule.cpp:190-251) on all host cores over a bounded sample."""
+    import numpy as np
+
+    import oracle as oracle_mod  # noqa: PLC0415 - checker only, CPU leg of the bench
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sample_heads = 2048
+    scale = (10.0 ** (-3.0 * rng.random((sample_heads, 1, 1)))).astype(np.float32)
+    states = (rng.standard_normal((sample_heads, 128, 128), dtype=np.float32) * scale)
+    states[rng.random(states.shape) < 0.01] = 0.0
+    if layout == "provider":
+        states = np.ascontiguousarray(states.transpose(0, 2, 1))
+    # warm-up pass, then repeat until the time budget is used
+    z, c, b = oracle_mod.quantize(states, layout, threads=cores)
+    oracle_mod.dequantize(z, c, b, layout=layout, threads=cores)
+    passes, start = 0, time.perf_counter()
+    while True:
+        z, c, b = oracle_mod.quantize(states, layout, threads=cores)
+        oracle_mod.dequantize(z, c, b, layout=layout, threads=cores)
+        passes += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= target_seconds:
+            break
+    return {
+        "value": passes * sample_heads / elapsed,
+        "unit": UNIT,
+        "cores": cores,
+        "kind": "port",
+        "sample": (f"{passes} passes of quantize+dequantize over {sample_heads} heads of the "
+                   f"benchmark distribution ({layout} layout), oracle/gdn_codec_oracle.c on "
+                   f"{cores} threads, {elapsed:.2f} s wall"),
+    }
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU codec path (the oracle's C
+    restatement of native/src quant-only arithmetic) on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle as oracle_mod  # noqa: PLC0415
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sample_heads = 4096
+    scale = (10.0 ** (-3.0 * rng.random((sample_heads, 1, 1)))).astype(np.float32)
+    states = rng.standard_normal((sample_heads, 128, 128), dtype=np.float32) * scale
+    states[rng.random(states.shape) < 0.01] = 0.0
+    if args.layout == "provider":
+        states = np.ascontiguousarray(states.transpose(0, 2, 1))
+
+    def step():
+        z, c, b = oracle_mod.quantize(states, args.layout, threads=cores)
+        oracle_mod.dequantize(z, c, b, layout=args.layout, threads=cores)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - start
+    value = args.steps * sample_heads / elapsed
+    sample = (f"each step: quantize+dequantize of {sample_heads} heads of the benchmark "
+              f"distribution (a bounded sample of config 2's 61,440 heads per GPU), "
+              f"oracle/gdn_codec_oracle.c on {cores} threads")
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "higher_is_better": True,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 sample: quantize+dequantize, CPU", "layout": args.layout,
+                   "heads_per_step": sample_heads},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.warmup < 3 and not args.profile:
+        raise SystemExit("--warmup must be >= 3")
+
+    import torch
+    import torch.distributed as dist
+
+    from gdn_state_codec import codec
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    slots = args.slots
+    heads = slots * LAYERS * HEADS
+    layout = args.layout
+    states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=0,
+                                     slot_base=rank * slots, device=device)
+    encoded = codec.empty_encoded((slots, LAYERS, HEADS), layout, device)
+    dense = torch.empty_like(states)
+    stream = torch.cuda.current_stream(device)
+
+    def step(events=None):
+        if events is not None:
+            events[0].record(stream)
+        codec.quantize(states, layout, out=encoded)
+        if events is not None:
+            events[1].record(stream)
+        codec.dequantize(encoded, out=dense)
+        if events is not None:
+            events[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    if args.profile:
+        for _ in range(args.steps):
+            step()
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile": True, "heads": heads, "steps": args.steps}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)  # let the sampler attach before the timed region
+    per_step = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                for _ in range(args.steps)]
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(per_step[i])
+    end.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    quant_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in per_step)
+    deq_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in per_step)
+    ms_per_step = elapsed_ms / args.steps
+    value = world * heads * args.steps / (elapsed_ms / 1e3)
+
+    # ---- end to end through the public API with host buffers -----------------
+    e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
+                      max_over_ranks, world)
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        dominant = "quantize" if quant_ms >= deq_ms else "dequantize"
+        dom_ms = max(quant_ms, deq_ms)
+        achieved = BYTES_PER_HEAD[dominant] * heads / (dom_ms / 1e3) / 1e9
+        traffic = committed_traffic(dominant, heads)
+        step_gbs = (BYTES_PER_HEAD["quantize"] + BYTES_PER_HEAD["dequantize"]) * heads / (
+            ms_per_step / 1e3) / 1e9
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded on device: N(0,1) x 10^(-3u) per head, "
+                                    "1% zeros)",
+            "config": {
+                "workload": "config2: 30 GDN layers x 64 slots x fp32 [32,128,128] per GPU, "
+                            "quantize (fused smoothing) + dequantize per step",
+                "layout": layout, "heads_per_gpu": heads, "global_batch": heads * world,
+                "parallelism": f"dp{world} (request slots sharded, no inter-GPU traffic)",
+                "l2": "inputs larger than L2 (9.1 GB touched per step vs 126 MB L2)",
+            },
+            "hbm_gbs_per_gpu": step_gbs,
+            "hbm_frac_per_gpu": step_gbs / peak,
+            "kernels_ms": {"quantize": quant_ms, "dequantize": deq_ms},
+            "roofline": {
+                "bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+                "peak_kind": f"{peak_kind} (hbm_gbs, burst copy)", "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "bytes_per_head": BYTES_PER_HEAD[dominant], "heads_per_launch": heads,
+            },
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        result["cpu_baseline"] = cpu_baseline(layout)
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def committed_traffic(kernel: str, heads: int):
+    """DRAM bytes per launch scaled from the committed ncu summary
+    (profiles/ncu_traffic.json: bytes per head measured on a capture)."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        per_head = json.loads(path.read_text())[kernel]["dram_bytes_per_head"]
+        return per_head * heads
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+def e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
+                max_over_ranks, world):
+    """Host fp32 states -> H2D -> quantize -> dequantize -> D2H fp32, per layer
+    chunk, with copies on their own streams so H2D, compute and D2H overlap."""
+    chunk_heads = HEADS * slots  # one layer's worth of heads per chunk
+    host_in = torch.empty(states.shape, dtype=torch.float32, pin_memory=True)
+    host_in.copy_(states)
+    host_out = torch.empty_like(host_in, pin_memory=True)
+    dev_in = torch.empty_like(states)
+    dev_out = torch.empty_like(states)
+    enc = codec.empty_encoded((slots, LAYERS, HEADS), layout, device)
+    flat = lambda t: t.view(-1, 128, 128)  # noqa: E731
+    views = [(flat(host_in)[i:i + chunk_heads], flat(dev_in)[i:i + chunk_heads],
+              flat(dev_out)[i:i + chunk_heads], flat(host_out)[i:i + chunk_heads],
+              i) for i in range(0, heads, chunk_heads)]
+    h2d = torch.cuda.Stream(device)
+    d2h = torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
+    enc_codes = enc.codes.view(-1, 128, 128)
+    enc_c = enc.smoothing.view(-1, 128)
+    enc_b = enc.scales.view(-1, 128)
+
+    def one_step():
+        for hin, din, dout, hout, i in views:
+            with torch.cuda.stream(h2d):
+                din.copy_(hin, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(h2d)
+            compute.wait_event(ready)
+            part = codec.EncodedStates(enc_codes[i:i + chunk_heads], enc_c[i:i + chunk_heads],
+                                       enc_b[i:i + chunk_heads], layout)
+            codec.quantize(din, layout, out=part)
+            codec.dequantize(part, out=dout)
+            done = torch.cuda.Event()
+            done.record(compute)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                hout.copy_(dout, non_blocking=True)
+        # the next step's first H2D may not overwrite inputs still in use
+        h2d.wait_stream(d2h)
+        h2d.wait_stream(compute)
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(3):
+        one_step()
+    torch.cuda.synchronize(device)
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(h2d)
+    for _ in range(steps):
+        one_step()
+    d2h.wait_stream(compute)
+    end.record(d2h)
+    torch.cuda.synchronize(device)
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end)) / steps
+    ok = bool(torch.equal(host_out[:1].to(device), codec.dequantize(
+        codec.quantize(states[:1].contiguous(), layout))))
+    nbytes = states.numel() * 4
+    return {"value": world * heads / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+            "steps": steps, "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+            "path": "gdn_state_codec.codec.quantize/dequantize (C ABI) per layer chunk, "
+                    "pinned host buffers, H2D/compute/D2H on separate streams",
+            "matches_device_path": ok}
+
+
+if __name__ == "__main__":
+    main()

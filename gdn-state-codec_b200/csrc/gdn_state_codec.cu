@@ -1,0 +1,418 @@
+// gdn_state_codec.cu -- the single translation unit of the B200 GDN state
+// codec library: the kernels (quantize.cuh, dequantize.cuh, projection.cuh,
+// synth.cuh) and the C ABI of include/statecentric/gdn_state_codec_kernel.h
+// over them: argument validation, per-device launch set-up and the launches.
+// The ABI allocates nothing and never synchronises the host.
+#include <cstdint>
+#include <mutex>
+
+#include "codec_device.cuh"
+#include "dequantize.cuh"
+#include "projection.cuh"
+#include "quantize.cuh"
+#include "synth.cuh"
+#include "statecentric/gdn_state_codec_kernel.h"
+#include "statecentric/gdn_state_codec_windowed_gdn_kernel.h"
+
+namespace gdnsc {
+
+namespace {
+
+constexpr int32_t kOk = 0;
+constexpr int32_t kBadArgs = 1;
+constexpr int32_t kLaunchFailed = 2;
+constexpr int32_t kSetupFailed = 3;
+constexpr int32_t kNotImplemented = 5;
+constexpr int kMaxDevices = 64;
+
+struct DeviceSetup {
+  bool ready = false;
+  int sms = 0;
+  int quantize_blocks[2][3] = {};  // [provider][mode] blocks per SM
+  int dequantize_blocks[2][2] = {};
+  int project_blocks[2][2] = {};
+};
+
+std::mutex g_setup_mutex;
+DeviceSetup g_setup[kMaxDevices];
+
+// Per-device one-time set-up (shared-memory opt-in and occupancy); guarded by
+// a mutex so concurrent host threads on one device are safe.
+const DeviceSetup* device_setup() {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  DeviceSetup& s = g_setup[device];
+  if (s.ready) return &s;
+  if (cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      s.sms <= 0) {
+    return nullptr;
+  }
+  for (int prov = 0; prov < 2; ++prov) {
+    for (int mode = 0; mode < 3; ++mode) {
+      if (prepare_quantize(prov != 0, mode, &s.quantize_blocks[prov][mode]) != cudaSuccess ||
+          s.quantize_blocks[prov][mode] < 1) {
+        return nullptr;
+      }
+    }
+    for (int comp = 0; comp < 2; ++comp) {
+      if (prepare_dequantize(prov != 0, comp != 0, &s.dequantize_blocks[prov][comp]) !=
+              cudaSuccess ||
+          s.dequantize_blocks[prov][comp] < 1) {
+        return nullptr;
+      }
+      if (prepare_project(prov != 0, comp != 0, &s.project_blocks[prov][comp]) != cudaSuccess ||
+          s.project_blocks[prov][comp] < 1) {
+        return nullptr;
+      }
+    }
+  }
+  s.ready = true;
+  return &s;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+int grid_for(uint64_t work_units, int sms, int blocks_per_sm) {
+  const uint64_t resident = static_cast<uint64_t>(sms) * static_cast<uint64_t>(blocks_per_sm);
+  return static_cast<int>(work_units < resident ? work_units : resident);
+}
+
+int32_t run_quantize(void* stream, bool provider, int mode, const float* state,
+                     const float* smoothing_in, float* smoothing, int8_t* codes, float* scales,
+                     uint64_t items, SlotMap map, uint32_t* status) {
+  const DeviceSetup* s = device_setup();
+  if (s == nullptr) return kSetupFailed;
+  QuantizeParams p{state, smoothing_in, smoothing, codes, scales, items, map, status};
+  const int grid = grid_for(items, s->sms, s->quantize_blocks[provider][mode]);
+  return launch_quantize(provider, mode, p, grid, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? kOk
+             : kLaunchFailed;
+}
+
+int32_t run_dequantize(void* stream, bool provider, const int8_t* codes, const float* smoothing,
+                       const float* scales, const float* ck, const float* cv, float* dense,
+                       uint64_t items, SlotMap map, uint32_t* status) {
+  const DeviceSetup* s = device_setup();
+  if (s == nullptr) return kSetupFailed;
+  const bool comp = ck != nullptr;
+  DequantizeParams p{codes, smoothing, scales, ck, cv, dense, items, map, status};
+  const int grid = grid_for(items, s->sms, s->dequantize_blocks[provider][comp]);
+  return launch_dequantize(provider, p, grid, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? kOk
+             : kLaunchFailed;
+}
+
+int32_t run_project(void* stream, bool provider, const int8_t* codes, const float* smoothing,
+                    const float* scales, const float* ck, const float* cv,
+                    const uint16_t* queries, float* outputs, uint64_t items, SlotMap map,
+                    uint32_t* status) {
+  const DeviceSetup* s = device_setup();
+  if (s == nullptr) return kSetupFailed;
+  const bool comp = ck != nullptr;
+  ProjectParams p{codes, smoothing, scales, ck, cv, queries, outputs, items, map, status};
+  const uint64_t blocks = (items + 3) / 4;  // four warps (heads) per block
+  const int grid = grid_for(blocks, s->sms, s->project_blocks[provider][comp]);
+  return launch_project(provider, p, grid, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? kOk
+             : kLaunchFailed;
+}
+
+bool compensators_ok(const float* ck, const float* cv) {
+  if ((ck == nullptr) != (cv == nullptr)) return false;
+  return ck == nullptr || (aligned16(ck) && aligned16(cv));
+}
+
+bool indexed_ok(uint32_t layout, const int32_t* slot_ids, uint32_t count,
+                uint32_t heads_per_slot, uint32_t num_slots) {
+  return layout <= 1u && slot_ids != nullptr && count != 0u && heads_per_slot != 0u &&
+         num_slots != 0u && (reinterpret_cast<uintptr_t>(slot_ids) & 3u) == 0;
+}
+
+}  // namespace
+}  // namespace gdnsc
+
+using gdnsc::SlotMap;
+using gdnsc::aligned16;
+using gdnsc::aligned8;
+
+extern "C" {
+
+// ---- Reference entry points -------------------------------------------------
+
+int32_t statecentric_gdn_state_codec_smoothing_launch_v1(void* stream, const float* residual,
+                                                         float* smoothing) {
+  if (residual == nullptr || smoothing == nullptr || !aligned16(residual) ||
+      !aligned16(smoothing)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, false, gdnsc::kSmoothingOnly, residual, nullptr, smoothing,
+                             nullptr, nullptr, 1, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_provider_smoothing_launch_v2(void* stream,
+                                                                  const float* provider_state,
+                                                                  float* smoothing,
+                                                                  uint32_t states) {
+  if (provider_state == nullptr || smoothing == nullptr || states == 0u ||
+      !aligned16(provider_state) || !aligned16(smoothing)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, true, gdnsc::kSmoothingOnly, provider_state, nullptr,
+                             smoothing, nullptr, nullptr, states, SlotMap{nullptr, 1, 1},
+                             nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_quantize_launch_v1(void* stream, const float* residual,
+                                                        const float* smoothing,
+                                                        int8_t* quantized, float* value_scales) {
+  if (residual == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || !aligned16(residual) || !aligned16(smoothing) ||
+      !aligned16(quantized) || !aligned16(value_scales)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, false, gdnsc::kGivenSmoothing, residual, smoothing, nullptr,
+                             quantized, value_scales, 1, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_provider_quantize_launch_v2(
+    void* stream, const float* provider_state, const float* smoothing, int8_t* quantized,
+    float* value_scales, uint32_t states) {
+  if (provider_state == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || states == 0u || !aligned16(provider_state) ||
+      !aligned16(smoothing) || !aligned16(quantized) || !aligned16(value_scales)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, true, gdnsc::kGivenSmoothing, provider_state, smoothing,
+                             nullptr, quantized, value_scales, states, SlotMap{nullptr, 1, 1},
+                             nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_provider_initialize_launch_v3(
+    void* stream, const float* provider_state, float* smoothing, int8_t* quantized,
+    float* value_scales, uint32_t states) {
+  if (provider_state == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || states == 0u || !aligned16(provider_state) ||
+      !aligned16(smoothing) || !aligned16(quantized) || !aligned16(value_scales)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, true, gdnsc::kFused, provider_state, nullptr, smoothing,
+                             quantized, value_scales, states, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_dequantize_launch_v1(
+    void* stream, const int8_t* quantized, const float* smoothing, const float* value_scales,
+    const float* compensator_keys, const float* compensator_values, float* dense) {
+  // The reference's single-head launcher requires both compensators.
+  if (quantized == nullptr || smoothing == nullptr || value_scales == nullptr ||
+      compensator_keys == nullptr || compensator_values == nullptr || dense == nullptr ||
+      !aligned16(quantized) || !aligned16(smoothing) || !aligned16(value_scales) ||
+      !aligned16(dense) || !gdnsc::compensators_ok(compensator_keys, compensator_values)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_dequantize(stream, false, quantized, smoothing, value_scales,
+                               compensator_keys, compensator_values, dense, 1,
+                               SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+// ---- Batched extensions -------------------------------------------------------
+
+int32_t statecentric_gdn_state_codec_initialize_launch_v3(void* stream, const float* residual,
+                                                          float* smoothing, int8_t* quantized,
+                                                          float* value_scales, uint32_t states) {
+  if (residual == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || states == 0u || !aligned16(residual) || !aligned16(smoothing) ||
+      !aligned16(quantized) || !aligned16(value_scales)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, false, gdnsc::kFused, residual, nullptr, smoothing,
+                             quantized, value_scales, states, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+static int32_t dequantize_batched(void* stream, bool provider, const int8_t* quantized,
+                                  const float* smoothing, const float* value_scales,
+                                  const float* ck, const float* cv, float* dense,
+                                  uint32_t states) {
+  if (quantized == nullptr || smoothing == nullptr || value_scales == nullptr ||
+      dense == nullptr || states == 0u || !aligned16(quantized) || !aligned16(smoothing) ||
+      !aligned16(value_scales) || !aligned16(dense) || !gdnsc::compensators_ok(ck, cv)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_dequantize(stream, provider, quantized, smoothing, value_scales, ck, cv,
+                               dense, states, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_dequantize_launch_v2(
+    void* stream, const int8_t* quantized, const float* smoothing, const float* value_scales,
+    const float* compensator_keys, const float* compensator_values, float* dense,
+    uint32_t states) {
+  return dequantize_batched(stream, false, quantized, smoothing, value_scales, compensator_keys,
+                            compensator_values, dense, states);
+}
+
+int32_t statecentric_gdn_state_codec_provider_dequantize_launch_v2(
+    void* stream, const int8_t* quantized, const float* smoothing, const float* value_scales,
+    const float* compensator_keys, const float* compensator_values, float* dense,
+    uint32_t states) {
+  return dequantize_batched(stream, true, quantized, smoothing, value_scales, compensator_keys,
+                            compensator_values, dense, states);
+}
+
+static int32_t project_batched(void* stream, bool provider, const int8_t* residual,
+                               const float* smoothing, const float* scales, const float* ck,
+                               const float* cv, const uint16_t* queries, float* outputs,
+                               uint32_t states) {
+  if (residual == nullptr || smoothing == nullptr || scales == nullptr || queries == nullptr ||
+      outputs == nullptr || states == 0u || !aligned16(residual) || !aligned16(smoothing) ||
+      !aligned16(scales) || !aligned8(queries) || !aligned16(outputs) ||
+      !gdnsc::compensators_ok(ck, cv)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_project(stream, provider, residual, smoothing, scales, ck, cv, queries,
+                            outputs, states, SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_encoded_projection_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const float* compensator_keys, const float* compensator_values, const uint16_t* queries_bf16,
+    float* outputs, uint32_t states) {
+  return project_batched(stream, false, residual, smoothing, scales, compensator_keys,
+                         compensator_values, queries_bf16, outputs, states);
+}
+
+int32_t statecentric_gdn_state_codec_provider_encoded_projection_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const float* compensator_keys, const float* compensator_values, const uint16_t* queries_bf16,
+    float* outputs, uint32_t states) {
+  return project_batched(stream, true, residual, smoothing, scales, compensator_keys,
+                         compensator_values, queries_bf16, outputs, states);
+}
+
+// ---- Slot-indexed extensions ----------------------------------------------------
+
+int32_t statecentric_gdn_state_codec_initialize_indexed_launch_v1(
+    void* stream, uint32_t layout, const float* state_cache, float* smoothing_cache,
+    int8_t* codes_cache, float* scales_cache, const int32_t* slot_ids, uint32_t count,
+    uint32_t heads_per_slot, uint32_t num_slots, uint32_t* status) {
+  if (!gdnsc::indexed_ok(layout, slot_ids, count, heads_per_slot, num_slots) ||
+      state_cache == nullptr || smoothing_cache == nullptr || codes_cache == nullptr ||
+      scales_cache == nullptr || !aligned16(state_cache) || !aligned16(smoothing_cache) ||
+      !aligned16(codes_cache) || !aligned16(scales_cache)) {
+    return gdnsc::kBadArgs;
+  }
+  const uint64_t items = static_cast<uint64_t>(count) * heads_per_slot;
+  return gdnsc::run_quantize(stream, layout == 1u, gdnsc::kFused, state_cache, nullptr,
+                             smoothing_cache, codes_cache, scales_cache, items,
+                             SlotMap{slot_ids, heads_per_slot, num_slots}, status);
+}
+
+int32_t statecentric_gdn_state_codec_dequantize_indexed_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes_cache, const float* smoothing_cache,
+    const float* scales_cache, const float* compensator_keys_cache,
+    const float* compensator_values_cache, float* state_cache, const int32_t* slot_ids,
+    uint32_t count, uint32_t heads_per_slot, uint32_t num_slots, uint32_t* status) {
+  if (!gdnsc::indexed_ok(layout, slot_ids, count, heads_per_slot, num_slots) ||
+      codes_cache == nullptr || smoothing_cache == nullptr || scales_cache == nullptr ||
+      state_cache == nullptr || !aligned16(codes_cache) || !aligned16(smoothing_cache) ||
+      !aligned16(scales_cache) || !aligned16(state_cache) ||
+      !gdnsc::compensators_ok(compensator_keys_cache, compensator_values_cache)) {
+    return gdnsc::kBadArgs;
+  }
+  const uint64_t items = static_cast<uint64_t>(count) * heads_per_slot;
+  return gdnsc::run_dequantize(stream, layout == 1u, codes_cache, smoothing_cache, scales_cache,
+                               compensator_keys_cache, compensator_values_cache, state_cache,
+                               items, SlotMap{slot_ids, heads_per_slot, num_slots}, status);
+}
+
+int32_t statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes_cache, const float* smoothing_cache,
+    const float* scales_cache, const float* compensator_keys_cache,
+    const float* compensator_values_cache, const uint16_t* queries_bf16, float* outputs,
+    const int32_t* slot_ids, uint32_t count, uint32_t heads_per_slot, uint32_t num_slots,
+    uint32_t* status) {
+  if (!gdnsc::indexed_ok(layout, slot_ids, count, heads_per_slot, num_slots) ||
+      codes_cache == nullptr || smoothing_cache == nullptr || scales_cache == nullptr ||
+      queries_bf16 == nullptr || outputs == nullptr || !aligned16(codes_cache) ||
+      !aligned16(smoothing_cache) || !aligned16(scales_cache) || !aligned8(queries_bf16) ||
+      !aligned16(outputs) ||
+      !gdnsc::compensators_ok(compensator_keys_cache, compensator_values_cache)) {
+    return gdnsc::kBadArgs;
+  }
+  const uint64_t items = static_cast<uint64_t>(count) * heads_per_slot;
+  return gdnsc::run_project(stream, layout == 1u, codes_cache, smoothing_cache, scales_cache,
+                            compensator_keys_cache, compensator_values_cache, queries_bf16,
+                            outputs, items, SlotMap{slot_ids, heads_per_slot, num_slots}, status);
+}
+
+// ---- Status and synthetic inputs --------------------------------------------------
+
+int32_t statecentric_gdn_state_codec_device_error_v1(uint32_t* bits, int32_t clear) {
+  if (bits == nullptr) return gdnsc::kBadArgs;
+  if (cudaMemcpyFromSymbol(bits, gdnsc::g_device_error, sizeof(uint32_t)) != cudaSuccess) {
+    return gdnsc::kLaunchFailed;
+  }
+  if (clear != 0) {
+    const uint32_t zero = 0u;
+    if (cudaMemcpyToSymbol(gdnsc::g_device_error, &zero, sizeof(uint32_t)) != cudaSuccess) {
+      return gdnsc::kLaunchFailed;
+    }
+  }
+  return gdnsc::kOk;
+}
+
+int32_t statecentric_gdn_state_codec_synthesize_states_v1(void* stream, float* out,
+                                                          uint32_t layout, uint64_t seed,
+                                                          uint32_t slot_base, uint32_t slots,
+                                                          uint32_t layers,
+                                                          uint32_t heads_per_layer) {
+  if (out == nullptr || layout > 1u || slots == 0u || layers == 0u || heads_per_layer == 0u ||
+      !aligned16(out)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::SynthParams p{out, static_cast<uint64_t>(slots) * layers * heads_per_layer, seed,
+                       slot_base, layers, heads_per_layer, layout};
+  return gdnsc::launch_synth_states(p, s->sms, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? gdnsc::kOk
+             : gdnsc::kLaunchFailed;
+}
+
+int32_t statecentric_gdn_state_codec_synthesize_queries_v1(void* stream, uint16_t* out,
+                                                           uint64_t seed, uint32_t slot_base,
+                                                           uint32_t slots, uint32_t layers,
+                                                           uint32_t heads_per_layer) {
+  if (out == nullptr || slots == 0u || layers == 0u || heads_per_layer == 0u || !aligned8(out)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::SynthParams p{out, static_cast<uint64_t>(slots) * layers * heads_per_layer, seed,
+                       slot_base, layers, heads_per_layer, 0u};
+  return gdnsc::launch_synth_queries(p, s->sms, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? gdnsc::kOk
+             : gdnsc::kLaunchFailed;
+}
+
+// ---- Loader-compatibility entry points (windowed decode is not implemented) -----
+
+int32_t statecentric_gdn_state_codec_windowed_gdn_step_launch_v1(
+    void*, const int8_t*, const float*, const float*, const uint16_t*, const uint16_t*, float*,
+    uint16_t*, uint16_t*, uint32_t*, const float*, const uint16_t*, const uint16_t*,
+    const uint16_t*, const uint16_t*, float*, uint32_t) {
+  return gdnsc::kNotImplemented;
+}
+
+int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(
+    void*, const int8_t*, const float*, const float*, const uint16_t*, const uint16_t*, float*,
+    uint16_t*, uint16_t*, uint32_t*, int8_t*, float*, float*, uint16_t*, uint16_t*, float*,
+    uint32_t, uint32_t) {
+  return gdnsc::kNotImplemented;
+}
+
+}  // extern "C"

@@ -1,0 +1,390 @@
+# SPDX-License-Identifier: Apache-2.0
+"""Torch-facing API of the B200 GDN state codec.
+
+Every function validates its tensors, then enqueues one launch of the CUDA
+library through the C ABI on the tensors' device and current CUDA stream.
+Nothing here computes on the host; a non-zero status from the library raises
+``RuntimeError`` (the reference runtime's behaviour, runtime.py:514-517).
+
+Layouts (one head = one [128, 128] GDN recurrent-state matrix):
+  ``"capsule"``  [key, value]  -- reference capsule order, [H, d_k, d_v]
+  ``"provider"`` [value, key]  -- vLLM ssm_state order
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+
+KEY_DIMENSION = 128
+VALUE_DIMENSION = 128
+COMPENSATOR_RANK = 4
+ELEMENTS = KEY_DIMENSION * VALUE_DIMENSION
+LAYOUTS = {"capsule": 0, "provider": 1}
+PAD_SLOT_ID = -1
+
+
+@dataclass
+class EncodedStates:
+    """Quant-only encoded heads: int8 codes in the layout of the fp32 state
+    they encode, smoothing per key and scales per value (17,408 B per head)."""
+
+    codes: torch.Tensor
+    smoothing: torch.Tensor
+    scales: torch.Tensor
+    layout: str = "capsule"
+
+    @property
+    def heads(self) -> int:
+        return self.codes.numel() // ELEMENTS
+
+
+def _ptr(tensor: torch.Tensor | None):
+    return None if tensor is None else ctypes.c_void_p(tensor.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check(tensor: torch.Tensor, name: str, dtype: torch.dtype, last: tuple[int, ...],
+           device: torch.device | None = None) -> int:
+    if not isinstance(tensor, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if tensor.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {tensor.device})")
+    if device is not None and tensor.device != device:
+        raise ValueError(f"{name} is on {tensor.device}, expected {device}")
+    if tensor.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype} (got {tensor.dtype})")
+    if not tensor.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if tensor.dim() < len(last) or tuple(tensor.shape[-len(last):]) != last:
+        raise ValueError(f"{name} must end in shape {last} (got {tuple(tensor.shape)})")
+    count = 1
+    for size in tensor.shape[: tensor.dim() - len(last)]:
+        count *= size
+    return count
+
+
+def _layout(layout: str) -> int:
+    if layout not in LAYOUTS:
+        raise ValueError(f"layout must be 'capsule' or 'provider' (got {layout!r})")
+    return LAYOUTS[layout]
+
+
+def _status(name: str, status: int) -> None:
+    if status != 0:
+        raise RuntimeError(f"GDN State Codec {name} launch failed: {status}")
+
+
+def _heads_ok(heads: int) -> None:
+    if heads < 1:
+        raise ValueError("at least one state is required")
+    if heads >= 2**32:
+        raise ValueError("at most 2^32 - 1 states per launch")
+
+
+def _compensators(encoded_heads: int, device, keys, values):
+    if (keys is None) != (values is None):
+        raise ValueError("compensator_keys and compensator_values go together")
+    if keys is None:
+        return None, None
+    k = _check(keys, "compensator_keys", torch.float32, (KEY_DIMENSION, COMPENSATOR_RANK), device)
+    v = _check(values, "compensator_values", torch.float32,
+               (VALUE_DIMENSION, COMPENSATOR_RANK), device)
+    if k != encoded_heads or v != encoded_heads:
+        raise ValueError("compensators must have one [128, 4] block per state")
+    return keys, values
+
+
+def empty_encoded(heads_shape: tuple[int, ...], layout: str = "capsule",
+                  device: torch.device | str = "cuda") -> EncodedStates:
+    return EncodedStates(
+        codes=torch.empty((*heads_shape, KEY_DIMENSION, VALUE_DIMENSION), dtype=torch.int8,
+                          device=device),
+        smoothing=torch.empty((*heads_shape, KEY_DIMENSION), dtype=torch.float32, device=device),
+        scales=torch.empty((*heads_shape, VALUE_DIMENSION), dtype=torch.float32, device=device),
+        layout=layout,
+    )
+
+
+def _check_encoded(encoded: EncodedStates, device=None) -> int:
+    heads = _check(encoded.codes, "codes", torch.int8, (KEY_DIMENSION, VALUE_DIMENSION), device)
+    dev = encoded.codes.device
+    if _check(encoded.smoothing, "smoothing", torch.float32, (KEY_DIMENSION,), dev) != heads:
+        raise ValueError("smoothing must have one [128] vector per state")
+    if _check(encoded.scales, "scales", torch.float32, (VALUE_DIMENSION,), dev) != heads:
+        raise ValueError("scales must have one [128] vector per state")
+    _layout(encoded.layout)
+    return heads
+
+
+# ---------------------------------------------------------------------------
+# Dense batches.
+
+def quantize(states: torch.Tensor, layout: str = "capsule", *,
+             out: EncodedStates | None = None) -> EncodedStates:
+    """Fused smoothing + int8 quantize of every [128, 128] head in ``states``.
+
+    Capsule layout calls ``initialize_launch_v3``; provider layout calls the
+    plugin's ``provider_initialize_launch_v3``."""
+    heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    _heads_ok(heads)
+    code = _layout(layout)
+    if out is None:
+        out = empty_encoded(tuple(states.shape[:-2]), layout, states.device)
+    if _check_encoded(out, states.device) != heads or out.layout != layout:
+        raise ValueError("output buffers do not match the input states")
+    name = ("statecentric_gdn_state_codec_provider_initialize_launch_v3" if code
+            else "statecentric_gdn_state_codec_initialize_launch_v3")
+    with torch.cuda.device(states.device):
+        _status("quantize", _native.call(name, _stream(states.device), _ptr(states),
+                                         _ptr(out.smoothing), _ptr(out.codes), _ptr(out.scales),
+                                         heads))
+    return out
+
+
+def smoothing(states: torch.Tensor, layout: str = "provider",
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Smoothing only.  Provider layout: ``provider_smoothing_launch_v2`` over
+    all heads; capsule layout: ``smoothing_launch_v1`` once per head."""
+    heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    _heads_ok(heads)
+    code = _layout(layout)
+    if out is None:
+        out = torch.empty((*states.shape[:-2], KEY_DIMENSION), dtype=torch.float32,
+                          device=states.device)
+    if _check(out, "smoothing", torch.float32, (KEY_DIMENSION,), states.device) != heads:
+        raise ValueError("smoothing output must have one [128] vector per state")
+    with torch.cuda.device(states.device):
+        stream = _stream(states.device)
+        if code:
+            _status("smoothing", _native.call(
+                "statecentric_gdn_state_codec_provider_smoothing_launch_v2", stream,
+                _ptr(states), _ptr(out), heads))
+        else:
+            flat_s, flat_o = states.view(-1, ELEMENTS), out.view(-1, KEY_DIMENSION)
+            for h in range(heads):
+                _status("smoothing", _native.call(
+                    "statecentric_gdn_state_codec_smoothing_launch_v1", stream,
+                    _ptr(flat_s[h]), _ptr(flat_o[h])))
+    return out
+
+
+def quantize_with_smoothing(states: torch.Tensor, smoothing_in: torch.Tensor,
+                            layout: str = "provider", *,
+                            out: EncodedStates | None = None) -> EncodedStates:
+    """Quantize with the caller's smoothing.  Provider layout:
+    ``provider_quantize_launch_v2``; capsule: ``quantize_launch_v1`` per head."""
+    heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    _heads_ok(heads)
+    code = _layout(layout)
+    if _check(smoothing_in, "smoothing", torch.float32, (KEY_DIMENSION,), states.device) != heads:
+        raise ValueError("smoothing must have one [128] vector per state")
+    if out is None:
+        out = empty_encoded(tuple(states.shape[:-2]), layout, states.device)
+    _check_encoded(out, states.device)
+    out.smoothing.copy_(smoothing_in)
+    with torch.cuda.device(states.device):
+        stream = _stream(states.device)
+        if code:
+            _status("quantize", _native.call(
+                "statecentric_gdn_state_codec_provider_quantize_launch_v2", stream,
+                _ptr(states), _ptr(smoothing_in), _ptr(out.codes), _ptr(out.scales), heads))
+        else:
+            fs, fc = states.view(-1, ELEMENTS), smoothing_in.view(-1, KEY_DIMENSION)
+            fz, fb = out.codes.view(-1, ELEMENTS), out.scales.view(-1, VALUE_DIMENSION)
+            for h in range(heads):
+                _status("quantize", _native.call(
+                    "statecentric_gdn_state_codec_quantize_launch_v1", stream,
+                    _ptr(fs[h]), _ptr(fc[h]), _ptr(fz[h]), _ptr(fb[h])))
+    return out
+
+
+def dequantize(encoded: EncodedStates, *, compensator_keys: torch.Tensor | None = None,
+               compensator_values: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 reconstruction ((c * z) / 127) * b [+ K V^T], same layout as the codes."""
+    heads = _check_encoded(encoded)
+    _heads_ok(heads)
+    device = encoded.codes.device
+    ck, cv = _compensators(heads, device, compensator_keys, compensator_values)
+    if out is None:
+        out = torch.empty(encoded.codes.shape, dtype=torch.float32, device=device)
+    if _check(out, "dense", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION), device) != heads:
+        raise ValueError("dense output must have one head per encoded head")
+    name = ("statecentric_gdn_state_codec_provider_dequantize_launch_v2"
+            if encoded.layout == "provider" else "statecentric_gdn_state_codec_dequantize_launch_v2")
+    with torch.cuda.device(device):
+        _status("dequantize", _native.call(
+            name, _stream(device), _ptr(encoded.codes), _ptr(encoded.smoothing),
+            _ptr(encoded.scales), _ptr(ck), _ptr(cv), _ptr(out), heads))
+    return out
+
+
+def encoded_projection(encoded: EncodedStates, queries: torch.Tensor, *,
+                       compensator_keys: torch.Tensor | None = None,
+                       compensator_values: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """o[h] = dequant(S_h)^T q_h from the int8 codes; q bf16 [..., 128] -> fp32."""
+    heads = _check_encoded(encoded)
+    _heads_ok(heads)
+    device = encoded.codes.device
+    if _check(queries, "queries", torch.bfloat16, (KEY_DIMENSION,), device) != heads:
+        raise ValueError("queries must have one [128] bf16 vector per state")
+    ck, cv = _compensators(heads, device, compensator_keys, compensator_values)
+    if out is None:
+        out = torch.empty(queries.shape, dtype=torch.float32, device=device)
+    if _check(out, "outputs", torch.float32, (VALUE_DIMENSION,), device) != heads:
+        raise ValueError("outputs must have one [128] vector per state")
+    name = ("statecentric_gdn_state_codec_provider_encoded_projection_launch_v1"
+            if encoded.layout == "provider"
+            else "statecentric_gdn_state_codec_encoded_projection_launch_v1")
+    with torch.cuda.device(device):
+        _status("encoded projection", _native.call(
+            name, _stream(device), _ptr(encoded.codes), _ptr(encoded.smoothing),
+            _ptr(encoded.scales), _ptr(ck), _ptr(cv), _ptr(queries), _ptr(out), heads))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Slot-indexed caches ([num_slots, heads_per_slot, ...], slot-major).
+
+def _slot_geometry(cache_heads: int, cache: torch.Tensor, slot_ids: torch.Tensor,
+                   heads_per_slot: int) -> tuple[int, int]:
+    if heads_per_slot < 1 or cache_heads % heads_per_slot:
+        raise ValueError("cache head count must be a multiple of heads_per_slot")
+    if (not isinstance(slot_ids, torch.Tensor) or slot_ids.dtype != torch.int32
+            or slot_ids.dim() != 1 or not slot_ids.is_contiguous()
+            or slot_ids.device != cache.device):
+        raise ValueError("slot_ids must be a contiguous 1-D int32 tensor on the cache's device")
+    count = slot_ids.numel()
+    if count < 1:
+        raise ValueError("at least one slot id is required")
+    if cache_heads // heads_per_slot >= 2**31:
+        raise ValueError("too many slots for int32 slot ids")
+    return count, cache_heads // heads_per_slot
+
+
+def quantize_indexed(state_cache: torch.Tensor, encoded_cache: EncodedStates,
+                     slot_ids: torch.Tensor, heads_per_slot: int, *,
+                     status: torch.Tensor | None = None) -> EncodedStates:
+    """Encode the listed slots of ``state_cache`` into the same slots of
+    ``encoded_cache``.  Ids of -1 are skipped; out-of-range ids are skipped and
+    set bit 0 of ``status`` (int32 device scalar, optional)."""
+    cache_heads = _check(state_cache, "state_cache", torch.float32,
+                         (KEY_DIMENSION, VALUE_DIMENSION))
+    device = state_cache.device
+    if _check_encoded(encoded_cache, device) != cache_heads:
+        raise ValueError("encoded cache must match the state cache")
+    count, num_slots = _slot_geometry(cache_heads, state_cache, slot_ids, heads_per_slot)
+    with torch.cuda.device(device):
+        _status("indexed quantize", _native.call(
+            "statecentric_gdn_state_codec_initialize_indexed_launch_v1", _stream(device),
+            LAYOUTS[encoded_cache.layout], _ptr(state_cache), _ptr(encoded_cache.smoothing),
+            _ptr(encoded_cache.codes), _ptr(encoded_cache.scales), _ptr(slot_ids), count,
+            heads_per_slot, num_slots, _ptr(status)))
+    return encoded_cache
+
+
+def dequantize_indexed(encoded_cache: EncodedStates, state_cache: torch.Tensor,
+                       slot_ids: torch.Tensor, heads_per_slot: int, *,
+                       compensator_keys: torch.Tensor | None = None,
+                       compensator_values: torch.Tensor | None = None,
+                       status: torch.Tensor | None = None) -> torch.Tensor:
+    cache_heads = _check_encoded(encoded_cache)
+    device = encoded_cache.codes.device
+    if _check(state_cache, "state_cache", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION),
+              device) != cache_heads:
+        raise ValueError("state cache must match the encoded cache")
+    ck, cv = _compensators(cache_heads, device, compensator_keys, compensator_values)
+    count, num_slots = _slot_geometry(cache_heads, state_cache, slot_ids, heads_per_slot)
+    with torch.cuda.device(device):
+        _status("indexed dequantize", _native.call(
+            "statecentric_gdn_state_codec_dequantize_indexed_launch_v1", _stream(device),
+            LAYOUTS[encoded_cache.layout], _ptr(encoded_cache.codes),
+            _ptr(encoded_cache.smoothing), _ptr(encoded_cache.scales), _ptr(ck), _ptr(cv),
+            _ptr(state_cache), _ptr(slot_ids), count, heads_per_slot, num_slots, _ptr(status)))
+    return state_cache
+
+
+def encoded_projection_indexed(encoded_cache: EncodedStates, queries: torch.Tensor,
+                               slot_ids: torch.Tensor, heads_per_slot: int, *,
+                               compensator_keys: torch.Tensor | None = None,
+                               compensator_values: torch.Tensor | None = None,
+                               out: torch.Tensor | None = None,
+                               status: torch.Tensor | None = None) -> torch.Tensor:
+    """Projection gathered by slot: queries / outputs are compact
+    [count, heads_per_slot, 128]; padded or invalid entries output zeros."""
+    cache_heads = _check_encoded(encoded_cache)
+    device = encoded_cache.codes.device
+    ck, cv = _compensators(cache_heads, device, compensator_keys, compensator_values)
+    count, num_slots = _slot_geometry(cache_heads, encoded_cache.codes, slot_ids, heads_per_slot)
+    if _check(queries, "queries", torch.bfloat16, (KEY_DIMENSION,), device) != count * heads_per_slot:
+        raise ValueError("queries must be [count, heads_per_slot, 128] bf16")
+    if out is None:
+        out = torch.empty(queries.shape, dtype=torch.float32, device=device)
+    if _check(out, "outputs", torch.float32, (VALUE_DIMENSION,), device) != count * heads_per_slot:
+        raise ValueError("outputs must be [count, heads_per_slot, 128] fp32")
+    with torch.cuda.device(device):
+        _status("indexed encoded projection", _native.call(
+            "statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1", _stream(device),
+            LAYOUTS[encoded_cache.layout], _ptr(encoded_cache.codes),
+            _ptr(encoded_cache.smoothing), _ptr(encoded_cache.scales), _ptr(ck), _ptr(cv),
+            _ptr(queries), _ptr(out), _ptr(slot_ids), count, heads_per_slot, num_slots,
+            _ptr(status)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Status and synthetic inputs.
+
+def device_error(device: torch.device | str | int = "cuda", clear: bool = False) -> int:
+    """Sticky error bits of the device: 1 = invalid slot id, 2 = wait timeout."""
+    bits = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        _status("device error query", _native.call(
+            "statecentric_gdn_state_codec_device_error_v1", ctypes.byref(bits), int(clear)))
+    return int(bits.value)
+
+
+def synthesize_states(slots: int, layers: int, heads_per_layer: int, *,
+                      layout: str = "capsule", seed: int = 0, slot_base: int = 0,
+                      device: torch.device | str = "cuda",
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Seeded GDN-like states [slots, layers, heads, 128, 128] generated on the
+    device; slot ``slot_base + i`` is the same on any device and any shard."""
+    code = _layout(layout)
+    if out is None:
+        out = torch.empty((slots, layers, heads_per_layer, KEY_DIMENSION, VALUE_DIMENSION),
+                          dtype=torch.float32, device=device)
+    heads = _check(out, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    if heads != slots * layers * heads_per_layer:
+        raise ValueError("output does not hold slots * layers * heads_per_layer heads")
+    with torch.cuda.device(out.device):
+        _status("synthesize states", _native.call(
+            "statecentric_gdn_state_codec_synthesize_states_v1", _stream(out.device), _ptr(out),
+            code, seed, slot_base, slots, layers, heads_per_layer))
+    return out
+
+
+def synthesize_queries(slots: int, layers: int, heads_per_layer: int, *, seed: int = 0,
+                       slot_base: int = 0, device: torch.device | str = "cuda",
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """Seeded bf16 queries [slots, layers, heads, 128], L2-normalised per head."""
+    if out is None:
+        out = torch.empty((slots, layers, heads_per_layer, KEY_DIMENSION), dtype=torch.bfloat16,
+                          device=device)
+    heads = _check(out, "queries", torch.bfloat16, (KEY_DIMENSION,))
+    if heads != slots * layers * heads_per_layer:
+        raise ValueError("output does not hold slots * layers * heads_per_layer queries")
+    with torch.cuda.device(out.device):
+        _status("synthesize queries", _native.call(
+            "statecentric_gdn_state_codec_synthesize_queries_v1", _stream(out.device), _ptr(out),
+            seed, slot_base, slots, layers, heads_per_layer))
+    return out

@@ -1,0 +1,192 @@
+/*
+ * gdn_state_codec_kernel.h -- C ABI of the B200 (sm_100a) GDN state codec.
+ *
+ * Drop-in boundary for the quant-only hot path of vLLM-HUST/gdn-state-codec:
+ * every entry point the reference declares in native/include/statecentric/
+ * gdn_state_codec_kernel.h is kept with the same name, argument order,
+ * argument meaning and return convention; the library files that carry them
+ * keep the reference's names (libstatecentric_gdn_state_codec_*.so, loaded
+ * by src/gdn_state_codec/runtime.py:55-237).
+ *
+ * Conventions shared by every entry point:
+ *  - `stream` is a cudaStream_t.  NULL means the legacy default stream (the
+ *    reference rejected a NULL aclrtStream; CUDA's NULL stream is valid).
+ *  - All pointers are device pointers owned by the caller; launches allocate
+ *    and free nothing and never synchronise the host.  Buffers of 4-byte or
+ *    wider elements must be 16-byte aligned (torch allocations are).
+ *  - One state ("head") is one [128 x 128] fp32 matrix.  Capsule layout is
+ *    [key, value] (reference capsule order, [heads, d_k, d_v]); provider
+ *    layout is [value, key] (vLLM ssm_state order).  Codes use the same
+ *    layout as the fp32 state they encode; smoothing is per key [128],
+ *    value scales are per value [128], compensators are [128][4] fp32.
+ *  - Return values: 0 = enqueued; 1 = rejected arguments (null pointer,
+ *    zero count, misalignment, bad layout flag); 2 = the CUDA launch failed;
+ *    3 = device query or kernel set-up failed; 5 = entry point exists only
+ *    for loader compatibility and is not implemented by this backend.
+ *  - `states` may be any value >= 1 (the reference's Ascend launchers
+ *    capped it at 64 per launch; this is a documented superset).
+ *  - Results are bit-identical to the reference's portable C++ codec
+ *    (native/src/gdn_state_codec_state_capsule.cpp) for finite inputs and
+ *    positive finite smoothing; non-finite inputs give unspecified codes.
+ */
+#ifndef STATECENTRIC_GDN_STATE_CODEC_KERNEL_H_
+#define STATECENTRIC_GDN_STATE_CODEC_KERNEL_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Reference entry points (gdn_state_codec_kernel.h:5-36) ------------- */
+
+/* One capsule-layout head: c[k] = sqrtf(max(mean_v |R[k][v]|, 1e-8)).
+ * Replaces gdn_state_codec_kernel.h:5-6 (libstatecentric_gdn_state_codec_
+ * smoothing_kernel.so). */
+int32_t statecentric_gdn_state_codec_smoothing_launch_v1(
+    void* stream, const float* residual, float* smoothing);
+
+/* `states` provider-layout heads [state][value][key] -> smoothing
+ * [state][key].  Replaces gdn_state_codec_kernel.h:11-14. */
+int32_t statecentric_gdn_state_codec_provider_smoothing_launch_v2(
+    void* stream, const float* provider_state, float* smoothing,
+    uint32_t states);
+
+/* One capsule-layout head quantized with the caller's smoothing: codes
+ * [key][value], value_scales [value].  Replaces gdn_state_codec_kernel.h:
+ * 16-18 (libstatecentric_gdn_state_codec_quantize_kernel.so). */
+int32_t statecentric_gdn_state_codec_quantize_launch_v1(
+    void* stream, const float* residual, const float* smoothing,
+    int8_t* quantized, float* value_scales);
+
+/* Provider-layout heads quantized with the caller's smoothing; codes keep
+ * the [state][value][key] order.  Replaces gdn_state_codec_kernel.h:20-23. */
+int32_t statecentric_gdn_state_codec_provider_quantize_launch_v2(
+    void* stream, const float* provider_state, const float* smoothing,
+    int8_t* quantized, float* value_scales, uint32_t states);
+
+/* Fused smoothing + quantize of provider-layout heads: the entry point the
+ * vLLM plugin calls (runtime.py:505-517).  One kernel instead of the
+ * reference's two (host/gdn_state_codec_provider_runtime.cpp:3-15).
+ * Replaces gdn_state_codec_kernel.h:28-31
+ * (libstatecentric_gdn_state_codec_provider_runtime.so). */
+int32_t statecentric_gdn_state_codec_provider_initialize_launch_v3(
+    void* stream, const float* provider_state, float* smoothing,
+    int8_t* quantized, float* value_scales, uint32_t states);
+
+/* One capsule-layout head: dense = ((c*z)/127)*b + sum_r K[k][r] V[v][r].
+ * compensator_keys / compensator_values are [128][4] fp32.  Replaces
+ * gdn_state_codec_kernel.h:33-36
+ * (libstatecentric_gdn_state_codec_dequantize_kernel.so). */
+int32_t statecentric_gdn_state_codec_dequantize_launch_v1(
+    void* stream, const int8_t* quantized, const float* smoothing,
+    const float* value_scales, const float* compensator_keys,
+    const float* compensator_values, float* dense);
+
+/* ---- Batched and slot-indexed extensions -------------------------------- */
+/* The reference exports these only in single-head or Ascend-window forms;
+ * the batched forms below follow the same conventions. */
+
+/* Fused smoothing + quantize of `states` capsule-layout heads
+ * [state][key][value] (capsule counterpart of provider_initialize_launch_v3,
+ * capsule.cpp:190-225 per head). */
+int32_t statecentric_gdn_state_codec_initialize_launch_v3(
+    void* stream, const float* residual, float* smoothing, int8_t* quantized,
+    float* value_scales, uint32_t states);
+
+/* Batched dequantize, capsule layout.  Compensators may both be NULL (the
+ * quant-only format, the plugin's default `quant_only` initializer); if one
+ * is non-NULL both must be.  Batched form of dequantize_launch_v1. */
+int32_t statecentric_gdn_state_codec_dequantize_launch_v2(
+    void* stream, const int8_t* quantized, const float* smoothing,
+    const float* value_scales, const float* compensator_keys,
+    const float* compensator_values, float* dense, uint32_t states);
+
+/* Batched dequantize, provider layout: codes [state][value][key] -> dense
+ * [state][value][key] (runtime.py:550-561 `reconstruct`). */
+int32_t statecentric_gdn_state_codec_provider_dequantize_launch_v2(
+    void* stream, const int8_t* quantized, const float* smoothing,
+    const float* value_scales, const float* compensator_keys,
+    const float* compensator_values, float* dense, uint32_t states);
+
+/* Encoded projection from capsule-layout codes: outputs[s][v] =
+ * (dequant(S_s)^T q_s)[v] computed from the codes without materialising the
+ * fp32 state (ReadWindowState boundary term, capsule.cpp:281-304).  queries
+ * are bf16 [state][128]; outputs fp32 [state][128].  Compensators nullable
+ * as above.  Added to libstatecentric_gdn_state_codec_encoded_projection_
+ * kernel.so (native/ascendc/gdn_state_codec/CMakeLists.txt:60-61), whose
+ * reference exports are the Ascend window/Cube pieces
+ * (gdn_state_codec_windowed_gdn_kernel.h:113-169). */
+int32_t statecentric_gdn_state_codec_encoded_projection_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing,
+    const float* scales, const float* compensator_keys,
+    const float* compensator_values, const uint16_t* queries_bf16,
+    float* outputs, uint32_t states);
+
+/* Encoded projection from provider-layout codes [state][value][key] (the
+ * plugin's encoded residual order, runtime.py:406-409). */
+int32_t statecentric_gdn_state_codec_provider_encoded_projection_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing,
+    const float* scales, const float* compensator_keys,
+    const float* compensator_values, const uint16_t* queries_bf16,
+    float* outputs, uint32_t states);
+
+/* Slot-indexed forms.  The caches hold `num_slots` slots of
+ * `heads_per_slot` heads each (slot-major: head index slot*heads_per_slot+h).
+ * `slot_ids` is a device array of `count` int32 ids (any order, may repeat
+ * only for read-only use); id -1 (PAD_SLOT_ID) is skipped; ids outside
+ * [-1, num_slots) are skipped and set bit 1 in *status (device uint32,
+ * optional) and in the library's sticky error word.  `layout` is 0 for
+ * capsule, 1 for provider.  The vLLM runtime range-checks its cache index on
+ * the host (runtime.py:607-608); these kernels check on the device instead. */
+
+/* state_cache -> (smoothing, codes, scales) caches at the listed slots. */
+int32_t statecentric_gdn_state_codec_initialize_indexed_launch_v1(
+    void* stream, uint32_t layout, const float* state_cache,
+    float* smoothing_cache, int8_t* codes_cache, float* scales_cache,
+    const int32_t* slot_ids, uint32_t count, uint32_t heads_per_slot,
+    uint32_t num_slots, uint32_t* status);
+
+/* (codes, smoothing, scales[, compensators]) caches -> state_cache at the
+ * listed slots. */
+int32_t statecentric_gdn_state_codec_dequantize_indexed_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes_cache,
+    const float* smoothing_cache, const float* scales_cache,
+    const float* compensator_keys_cache, const float* compensator_values_cache,
+    float* state_cache, const int32_t* slot_ids, uint32_t count,
+    uint32_t heads_per_slot, uint32_t num_slots, uint32_t* status);
+
+/* Encoded projection gathered by slot: queries_bf16 and outputs are compact
+ * [count][heads_per_slot][128]; padded or invalid entries output zeros. */
+int32_t statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes_cache,
+    const float* smoothing_cache, const float* scales_cache,
+    const float* compensator_keys_cache, const float* compensator_values_cache,
+    const uint16_t* queries_bf16, float* outputs, const int32_t* slot_ids,
+    uint32_t count, uint32_t heads_per_slot, uint32_t num_slots,
+    uint32_t* status);
+
+/* ---- Library status and benchmark support ------------------------------- */
+
+/* Read (and with clear != 0 reset) the sticky per-device error word of the
+ * current device: bit 0 = an invalid slot id was seen, bit 1 = a bounded
+ * device wait expired.  Synchronous. */
+int32_t statecentric_gdn_state_codec_device_error_v1(uint32_t* bits, int32_t clear);
+
+/* Seeded synthetic inputs (benchmark and test support): `slots` slots of
+ * `layers` x `heads_per_layer` heads starting at global slot `slot_base`.
+ * States follow x ~ N(0,1) * 10^(-3u), u ~ U[0,1) per head, 1% zeros, in
+ * `layout` order; queries are N(0,1), L2-normalised per head, bf16. */
+int32_t statecentric_gdn_state_codec_synthesize_states_v1(
+    void* stream, float* out, uint32_t layout, uint64_t seed,
+    uint32_t slot_base, uint32_t slots, uint32_t layers,
+    uint32_t heads_per_layer);
+int32_t statecentric_gdn_state_codec_synthesize_queries_v1(
+    void* stream, uint16_t* out, uint64_t seed, uint32_t slot_base,
+    uint32_t slots, uint32_t layers, uint32_t heads_per_layer);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* STATECENTRIC_GDN_STATE_CODEC_KERNEL_H_ */

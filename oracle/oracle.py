@@ -1,0 +1,265 @@
+"""CPU oracle for the GDN state codec hot path -- TEST INFRASTRUCTURE ONLY.
+
+Thin numpy/ctypes front end over ``liboracle.so`` (the C restatement in
+``gdn_codec_oracle.c``) and, when it has been built in this container, over
+``_ref/libgdn_ref.so`` (the reference's own portable library from
+native/src of vLLM-HUST/gdn-state-codec, wrapped by ``ref_shim.cpp``).
+
+Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
+``bench.py`` import this module, and only as the checker; the product
+library never routes through it.
+
+Layouts (one head = one [128,128] GDN state matrix):
+  capsule  [key, value]  -- native/src capsule layout, BASELINE's [H, d_k, d_v]
+  provider [value, key]  -- vLLM's ssm_state layout (runtime.py:460-471)
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+ORACLE_DIR = Path(__file__).resolve().parent
+LIB_PATH = ORACLE_DIR / "liboracle.so"
+REF_LIB_PATH = ORACLE_DIR / "_ref" / "libgdn_ref.so"
+RANK = 4
+
+_lib = None
+_ref = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+
+
+def _ptr(array: np.ndarray | None, ctype):
+    if array is None:
+        return ctypes.cast(None, ctype)
+    assert array.flags["C_CONTIGUOUS"]
+    return array.ctypes.data_as(ctype)
+
+
+def build() -> None:
+    """Compile liboracle.so (and _ref/ when the reference tree is present)."""
+    import subprocess
+
+    subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
+    ref_root = Path(os.environ.get("GDN_REFERENCE_ROOT", "/root/reference"))
+    if (ref_root / "native" / "src").is_dir():
+        subprocess.run(
+            ["make", "-s", "-C", str(ORACLE_DIR), "ref", f"REF={ref_root}"],
+            check=True,
+        )
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.is_file():
+            raise RuntimeError(f"oracle library not built: {LIB_PATH}")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        u64, u32, c_int = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int
+        handle.oracle_smoothing.argtypes = [_f32p, u64, u32, u32, c_int, _f32p]
+        handle.oracle_quantize_given_smoothing.argtypes = [
+            _f32p, _f32p, u64, u32, u32, c_int, _i8p, _f32p]
+        handle.oracle_quantize.argtypes = [
+            _f32p, u64, u32, u32, c_int, _f32p, _i8p, _f32p]
+        handle.oracle_dequantize.argtypes = [
+            _i8p, _f32p, _f32p, _f32p, _f32p, u64, u32, u32, c_int, _f32p]
+        handle.oracle_project.argtypes = [
+            _i8p, _f32p, _f32p, _f32p, _f32p, _f32p, u64, u32, u32, c_int, _f32p]
+        handle.oracle_provider_to_capsule.argtypes = [_f32p, u64, u32, u32, _f32p]
+        handle.oracle_capsule_to_provider.argtypes = [_f32p, u64, u32, u32, _f32p]
+        handle.oracle_quantize_mt.argtypes = [
+            _f32p, u64, u32, u32, c_int, _f32p, _i8p, _f32p, c_int]
+        handle.oracle_quantize_mt.restype = c_int
+        handle.oracle_dequantize_mt.argtypes = [
+            _i8p, _f32p, _f32p, u64, u32, u32, c_int, _f32p, c_int]
+        handle.oracle_dequantize_mt.restype = c_int
+        handle.oracle_project_mt.argtypes = [
+            _i8p, _f32p, _f32p, _f32p, u64, u32, u32, c_int, _f32p, c_int]
+        handle.oracle_project_mt.restype = c_int
+        _lib = handle
+    return _lib
+
+
+def _geometry(state: np.ndarray, layout: str) -> tuple[int, int, int, int]:
+    if state.ndim != 3:
+        raise ValueError("expected [heads, rows, cols]")
+    heads, rows, cols = state.shape
+    provider = 1 if layout == "provider" else 0
+    keys, values = (cols, rows) if provider else (rows, cols)
+    return heads, keys, values, provider
+
+
+def smoothing(state: np.ndarray, layout: str = "capsule") -> np.ndarray:
+    state = np.ascontiguousarray(state, dtype=np.float32)
+    heads, keys, values, provider = _geometry(state, layout)
+    c = np.empty((heads, keys), np.float32)
+    lib().oracle_smoothing(_ptr(state, _f32p), heads, keys, values, provider,
+                           _ptr(c, _f32p))
+    return c
+
+
+def quantize(state: np.ndarray, layout: str = "capsule", smoothing_in=None,
+             threads: int = 1):
+    """Fused smoothing + quantize: returns (codes, smoothing, scales).
+
+    With ``smoothing_in`` the smoothing is taken as given (the reference's
+    quantize_launch_v1 / provider_quantize_launch_v2 contract)."""
+    state = np.ascontiguousarray(state, dtype=np.float32)
+    heads, keys, values, provider = _geometry(state, layout)
+    codes = np.empty(state.shape, np.int8)
+    b = np.empty((heads, values), np.float32)
+    if smoothing_in is not None:
+        c = np.ascontiguousarray(smoothing_in, dtype=np.float32).reshape(heads, keys)
+        lib().oracle_quantize_given_smoothing(
+            _ptr(state, _f32p), _ptr(c, _f32p), heads, keys, values, provider,
+            _ptr(codes, _i8p), _ptr(b, _f32p))
+        return codes, c, b
+    c = np.empty((heads, keys), np.float32)
+    if threads > 1:
+        lib().oracle_quantize_mt(_ptr(state, _f32p), heads, keys, values, provider,
+                                 _ptr(c, _f32p), _ptr(codes, _i8p), _ptr(b, _f32p),
+                                 threads)
+    else:
+        lib().oracle_quantize(_ptr(state, _f32p), heads, keys, values, provider,
+                              _ptr(c, _f32p), _ptr(codes, _i8p), _ptr(b, _f32p))
+    return codes, c, b
+
+
+def dequantize(codes, c, b, compensator_keys=None, compensator_values=None,
+               layout: str = "capsule", threads: int = 1) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    heads, keys, values, provider = _geometry(codes, layout)
+    c = np.ascontiguousarray(c, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    out = np.empty(codes.shape, np.float32)
+    if threads > 1 and compensator_keys is None:
+        lib().oracle_dequantize_mt(_ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p),
+                                   heads, keys, values, provider, _ptr(out, _f32p),
+                                   threads)
+        return out
+    ck = None if compensator_keys is None else np.ascontiguousarray(
+        compensator_keys, dtype=np.float32)
+    cv = None if compensator_values is None else np.ascontiguousarray(
+        compensator_values, dtype=np.float32)
+    lib().oracle_dequantize(_ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p),
+                            _ptr(ck, _f32p), _ptr(cv, _f32p), heads, keys, values,
+                            provider, _ptr(out, _f32p))
+    return out
+
+
+def project(codes, c, b, queries, compensator_keys=None, compensator_values=None,
+            layout: str = "capsule", threads: int = 1) -> np.ndarray:
+    """Encoded projection o[h, v] = (dequant(S_h)^T q_h)[v] from the codes."""
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    heads, keys, values, provider = _geometry(codes, layout)
+    c = np.ascontiguousarray(c, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    x = np.ascontiguousarray(queries, dtype=np.float32).reshape(heads, keys)
+    out = np.empty((heads, values), np.float32)
+    if threads > 1 and compensator_keys is None:
+        lib().oracle_project_mt(_ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p),
+                                _ptr(x, _f32p), heads, keys, values, provider,
+                                _ptr(out, _f32p), threads)
+        return out
+    ck = None if compensator_keys is None else np.ascontiguousarray(
+        compensator_keys, dtype=np.float32)
+    cv = None if compensator_values is None else np.ascontiguousarray(
+        compensator_values, dtype=np.float32)
+    lib().oracle_project(_ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p),
+                         _ptr(ck, _f32p), _ptr(cv, _f32p), _ptr(x, _f32p), heads,
+                         keys, values, provider, _ptr(out, _f32p))
+    return out
+
+
+def provider_to_capsule(provider: np.ndarray) -> np.ndarray:
+    provider = np.ascontiguousarray(provider, dtype=np.float32)
+    heads, values, keys = provider.shape
+    out = np.empty((heads, keys, values), np.float32)
+    lib().oracle_provider_to_capsule(_ptr(provider, _f32p), heads, keys, values,
+                                     _ptr(out, _f32p))
+    return out
+
+
+def capsule_to_provider(capsule: np.ndarray) -> np.ndarray:
+    capsule = np.ascontiguousarray(capsule, dtype=np.float32)
+    heads, keys, values = capsule.shape
+    out = np.empty((heads, values, keys), np.float32)
+    lib().oracle_capsule_to_provider(_ptr(capsule, _f32p), heads, keys, values,
+                                     _ptr(out, _f32p))
+    return out
+
+
+def rebuild_residual(dense: np.ndarray, compensator_keys: np.ndarray,
+                     compensator_values: np.ndarray) -> np.ndarray:
+    """Residual left after the reference's rank-4 fit, capsule.cpp:182-187.
+
+    The reference subtracts ``left * sv * right`` rank by rank; it stores
+    ``left * sv`` as the compensator key, so the same fp32 products
+    (K[k,r] * V[v,r], then one subtraction, no FMA) rebuild R exactly."""
+    r = np.array(dense, dtype=np.float32, copy=True)
+    ck = np.asarray(compensator_keys, np.float32)
+    cv = np.asarray(compensator_values, np.float32)
+    keys, values = r.shape
+    ck = ck.reshape(keys, RANK)
+    cv = cv.reshape(values, RANK)
+    for rank in range(RANK):
+        r -= np.outer(ck[:, rank], cv[:, rank]).astype(np.float32)
+    return r
+
+
+# --------------------------------------------------------------------------
+# The reference library itself (only where it was compiled from source here).
+
+def ref_available() -> bool:
+    return REF_LIB_PATH.is_file()
+
+
+def ref() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not REF_LIB_PATH.is_file():
+            raise RuntimeError(f"reference library not built: {REF_LIB_PATH}")
+        handle = ctypes.CDLL(str(REF_LIB_PATH))
+        u32 = ctypes.c_uint32
+        handle.ref_codec_head.argtypes = [
+            _f32p, u32, u32, _f32p, _i8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]
+        handle.ref_codec_head.restype = ctypes.c_int
+        handle.ref_provider_to_capsule.argtypes = [_f32p, u32, u32, _f32p]
+        handle.ref_provider_to_capsule.restype = ctypes.c_int
+        handle.ref_head_bytes.argtypes = [
+            u32, u32, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
+        handle.ref_head_bytes.restype = ctypes.c_int
+        _ref = handle
+    return _ref
+
+
+def ref_codec_head(dense: np.ndarray, query: np.ndarray | None = None) -> dict:
+    """Run the real reference codec on one capsule-layout head."""
+    dense = np.ascontiguousarray(dense, dtype=np.float32)
+    keys, values = dense.shape
+    out = {
+        "codes": np.empty((keys, values), np.int8),
+        "smoothing": np.empty(keys, np.float32),
+        "scales": np.empty(values, np.float32),
+        "compensator_keys": np.empty((keys, RANK), np.float32),
+        "compensator_values": np.empty((values, RANK), np.float32),
+        "dense_state": np.empty((keys, values), np.float32),
+        "projection": np.empty(values, np.float32),
+    }
+    q = None if query is None else np.ascontiguousarray(query, dtype=np.float32)
+    status = ref().ref_codec_head(
+        _ptr(dense, _f32p), keys, values, _ptr(q, _f32p),
+        _ptr(out["codes"], _i8p), _ptr(out["smoothing"], _f32p),
+        _ptr(out["scales"], _f32p), _ptr(out["compensator_keys"], _f32p),
+        _ptr(out["compensator_values"], _f32p), _ptr(out["dense_state"], _f32p),
+        _ptr(out["projection"], _f32p) if q is not None else _ptr(None, _f32p))
+    if status != 0:
+        raise ValueError("reference codec rejected the input")
+    if q is None:
+        del out["projection"]
+    return out

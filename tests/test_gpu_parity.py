@@ -1,0 +1,253 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI, against the CPU
+oracle (oracle/gdn_codec_oracle.c, pinned to the reference library by
+tests/test_oracle_golden.py) and against the reference's own golden vectors.
+
+Bar: int8 codes, smoothing, scales and slot
+indexing bit-exact; dequantised values and projection outputs within
+rtol 1e-5 / atol 1e-6 of the reference's fp32 results.  The kernels follow the
+reference's operation order, so these tests also assert bit equality of the
+floating-point outputs and report it separately from the tolerance check.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gdn_state_codec import codec
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+DEV = torch.device("cuda:0")
+
+
+def bits(x: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(x, np.float32).view(np.uint32)
+
+
+def assert_bit_exact(name: str, got: np.ndarray, want: np.ndarray) -> None:
+    if got.dtype == np.float32:
+        mismatches = int((bits(got) != bits(want)).sum())
+    else:
+        mismatches = int((got != want).sum())
+    assert mismatches == 0, f"{name}: {mismatches} of {got.size} elements differ"
+
+
+def assert_close_and_exact(name: str, got: np.ndarray, want: np.ndarray) -> None:
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL, err_msg=name)
+    # Same operation order as the reference -> identical values (+0 and -0
+    # compare equal here; the reference's sum order fixes them anyway).
+    assert np.array_equal(got, want), f"{name}: within tolerance but not identical"
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def batch():
+    """4096 heads of the benchmark distribution (64 slots x 2 layers x 32
+    heads), generated on the device in both layouts."""
+    torch.cuda.init()
+    cap = codec.synthesize_states(64, 2, 32, layout="capsule", seed=0, device=DEV)
+    prov = codec.synthesize_states(64, 2, 32, layout="provider", seed=0, device=DEV)
+    q = codec.synthesize_queries(64, 2, 32, seed=0, device=DEV)
+    torch.cuda.synchronize()
+    return cap, prov, q
+
+
+def test_synthesized_layouts_are_transposes(batch):
+    cap, prov, _ = batch
+    assert torch.equal(cap.transpose(-2, -1), prov)
+    host = to_np(cap).reshape(-1, 128, 128)
+    # 1% exact zeros, per-head scale in [1e-3, 1].
+    zero_fraction = float((host == 0).mean())
+    assert 0.008 < zero_fraction < 0.012
+    scale = np.abs(host).reshape(host.shape[0], -1).std(axis=1)
+    assert scale.min() > 5e-4 and scale.max() < 1.5
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_quantize_bit_exact(batch, layout):
+    states = batch[0] if layout == "capsule" else batch[1]
+    enc = codec.quantize(states, layout)
+    torch.cuda.synchronize()
+    host = to_np(states).reshape(-1, 128, 128)
+    z, c, b = oracle.quantize(host, layout, threads=8)
+    assert_bit_exact("smoothing", to_np(enc.smoothing).reshape(-1, 128), c)
+    assert_bit_exact("scales", to_np(enc.scales).reshape(-1, 128), b)
+    assert_bit_exact("codes", to_np(enc.codes).reshape(-1, 128, 128), z)
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_dequantize_bit_exact(batch, layout):
+    states = batch[0] if layout == "capsule" else batch[1]
+    enc = codec.quantize(states, layout)
+    dense = codec.dequantize(enc)
+    torch.cuda.synchronize()
+    want = oracle.dequantize(to_np(enc.codes).reshape(-1, 128, 128),
+                             to_np(enc.smoothing).reshape(-1, 128),
+                             to_np(enc.scales).reshape(-1, 128), layout=layout, threads=8)
+    got = to_np(dense).reshape(-1, 128, 128)
+    assert_close_and_exact("dense", got, want)
+    assert_bit_exact("dense bits", got, want)
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_encoded_projection(batch, layout):
+    states = batch[0] if layout == "capsule" else batch[1]
+    q = batch[2]
+    enc = codec.quantize(states, layout)
+    out = codec.encoded_projection(enc, q)
+    torch.cuda.synchronize()
+    want = oracle.project(to_np(enc.codes).reshape(-1, 128, 128),
+                          to_np(enc.smoothing).reshape(-1, 128),
+                          to_np(enc.scales).reshape(-1, 128),
+                          to_np(q.float()).reshape(-1, 128), layout=layout, threads=8)
+    got = to_np(out).reshape(-1, 128)
+    assert_close_and_exact("projection", got, want)
+    # Fused readout equals dequantize-then-matvec within the fp32 tolerance
+    # against an fp64 recomputation (survey c4: record the fp64 error too).
+    dense = to_np(codec.dequantize(enc)).reshape(-1, 128, 128).astype(np.float64)
+    qd = to_np(q.float()).reshape(-1, 128).astype(np.float64)
+    ref64 = (np.einsum("hkv,hk->hv", dense, qd) if layout == "capsule"
+             else np.einsum("hvk,hk->hv", dense, qd))
+    np.testing.assert_allclose(got, ref64, rtol=1e-4, atol=1e-5)
+
+
+def test_reference_golden_vectors(golden):
+    """Kernels against the reference library's own outputs (capsule layout):
+    the quantizer on the residual left by the reference's rank-4 fit must
+    reproduce the serialized boundary, and dequantize / projection with the
+    reference's compensators must reproduce DenseState() and ApplyToken()."""
+    g = golden["heads"]
+    n = g["dense"].shape[0]
+    residual = np.stack([oracle.rebuild_residual(g["dense"][i], g["compensator_keys"][i],
+                                                 g["compensator_values"][i]) for i in range(n)])
+    enc = codec.quantize(torch.from_numpy(residual).to(DEV), "capsule")
+    ck = torch.from_numpy(g["compensator_keys"]).to(DEV)
+    cv = torch.from_numpy(g["compensator_values"]).to(DEV)
+    q = torch.from_numpy(g["query"]).to(DEV).to(torch.bfloat16)
+    assert torch.equal(q.float().cpu(), torch.from_numpy(g["query"]))  # bf16-exact queries
+    dense = codec.dequantize(enc, compensator_keys=ck, compensator_values=cv)
+    proj = codec.encoded_projection(enc, q, compensator_keys=ck, compensator_values=cv)
+    torch.cuda.synchronize()
+    assert_bit_exact("codes", to_np(enc.codes), g["codes"])
+    assert_bit_exact("smoothing", to_np(enc.smoothing), g["smoothing"])
+    assert_bit_exact("scales", to_np(enc.scales), g["scales"])
+    assert_close_and_exact("DenseState", to_np(dense), g["dense_state"])
+    assert_close_and_exact("ApplyToken readout", to_np(proj), g["projection"])
+
+
+def test_reference_single_head_entry_points(golden):
+    """smoothing_launch_v1 / quantize_launch_v1 / dequantize_launch_v1 (the
+    reference's single-head capsule ABI) on the golden heads."""
+    g = golden["heads"]
+    residual = np.stack([oracle.rebuild_residual(g["dense"][i], g["compensator_keys"][i],
+                                                 g["compensator_values"][i])
+                         for i in range(g["dense"].shape[0])])
+    r = torch.from_numpy(residual).to(DEV)
+    c = codec.smoothing(r, "capsule")
+    enc = codec.quantize_with_smoothing(r, c, "capsule")
+    from gdn_state_codec import _native
+    import ctypes
+    dense = torch.empty_like(r)
+    ck = torch.from_numpy(g["compensator_keys"]).to(DEV)
+    cv = torch.from_numpy(g["compensator_values"]).to(DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for h in range(r.shape[0]):
+        status = _native.call(
+            "statecentric_gdn_state_codec_dequantize_launch_v1", stream,
+            ctypes.c_void_p(enc.codes[h].data_ptr()), ctypes.c_void_p(enc.smoothing[h].data_ptr()),
+            ctypes.c_void_p(enc.scales[h].data_ptr()), ctypes.c_void_p(ck[h].data_ptr()),
+            ctypes.c_void_p(cv[h].data_ptr()), ctypes.c_void_p(dense[h].data_ptr()))
+        assert status == 0
+    torch.cuda.synchronize()
+    assert_bit_exact("smoothing v1", to_np(c), g["smoothing"])
+    assert_bit_exact("codes v1", to_np(enc.codes), g["codes"])
+    assert_bit_exact("scales v1", to_np(enc.scales), g["scales"])
+    assert_close_and_exact("dequantize v1", to_np(dense), g["dense_state"])
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_two_stage_equals_fused(batch, layout):
+    """smoothing + quantize-with-smoothing (provider v2 pair / capsule v1
+    pair) equals the fused initializer (provider_runtime.cpp:3-15)."""
+    states = (batch[0] if layout == "capsule" else batch[1]).reshape(-1, 128, 128)[:256]
+    fused = codec.quantize(states, layout)
+    c = codec.smoothing(states, layout)
+    staged = codec.quantize_with_smoothing(states, c, layout)
+    torch.cuda.synchronize()
+    assert torch.equal(c, fused.smoothing)
+    assert torch.equal(staged.codes, fused.codes)
+    assert torch.equal(staged.scales, fused.scales)
+
+
+def _edge_heads(rng: np.random.Generator) -> np.ndarray:
+    heads = []
+    heads.append(np.zeros((128, 128), np.float32))                      # all zero
+    one = np.zeros((128, 128), np.float32); one[5, 77] = -3.25          # single nonzero
+    heads.append(one)
+    h = rng.standard_normal((128, 128)).astype(np.float32)
+    h[:, 3] = 0.0; h[9, :] = 0.0                                         # zero column and row
+    heads.append(h)
+    heads.append((rng.standard_normal((128, 128)) * 1e-30).astype(np.float32))  # tiny
+    heads.append((rng.standard_normal((128, 128)) * 1e-41).astype(np.float32))  # denormals
+    heads.append((rng.standard_normal((128, 128)) * 1e30).astype(np.float32))   # huge
+    wide = rng.standard_normal((128, 128)) * 10.0 ** rng.uniform(-30, 30, (128, 128))
+    heads.append(wide.astype(np.float32))                                # wild range
+    # Exact ties: rows share one multiset of magnitudes with mean 1/4, so
+    # c = 1/2 exactly and s = 2R; values (n + 1/2) * 2^-7 put s/b*127 on or
+    # next to rounding boundaries.
+    base = ((np.arange(128) % 127) + 0.5) * 2.0 ** -7
+    base = base * (0.25 / base.mean())
+    ties = np.stack([np.roll(base, k) for k in range(128)]).astype(np.float32)
+    ties *= np.where(rng.random((128, 128)) < 0.5, -1, 1).astype(np.float32)
+    heads.append(ties)
+    grid = (rng.integers(-127, 128, (128, 128)) * 2.0 ** -9).astype(np.float32)  # dyadic grid
+    heads.append(grid)
+    return np.stack(heads)
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_edge_cases_bit_exact(layout):
+    rng = np.random.default_rng(7)
+    cap = _edge_heads(rng)
+    host = cap if layout == "capsule" else np.ascontiguousarray(cap.transpose(0, 2, 1))
+    states = torch.from_numpy(host).to(DEV)
+    enc = codec.quantize(states, layout)
+    dense = codec.dequantize(enc)
+    q = torch.from_numpy(rng.standard_normal((host.shape[0], 128)).astype(np.float32)).to(DEV)
+    q = q.to(torch.bfloat16)
+    proj = codec.encoded_projection(enc, q)
+    torch.cuda.synchronize()
+    z, c, b = oracle.quantize(host, layout)
+    assert_bit_exact("edge smoothing", to_np(enc.smoothing), c)
+    assert_bit_exact("edge scales", to_np(enc.scales), b)
+    assert_bit_exact("edge codes", to_np(enc.codes), z)
+    assert_bit_exact("edge dense", to_np(dense), oracle.dequantize(z, c, b, layout=layout))
+    want = oracle.project(z, c, b, to_np(q.float()), layout=layout)
+    assert np.array_equal(to_np(proj), want, equal_nan=True)
+
+
+def test_random_compensators_bit_exact(batch):
+    """Full-codec format (rank-4 fp32 compensators) for both layouts."""
+    rng = np.random.default_rng(3)
+    for layout, states in (("capsule", batch[0]), ("provider", batch[1])):
+        s = states.reshape(-1, 128, 128)[:64].contiguous()
+        enc = codec.quantize(s, layout)
+        ck = torch.from_numpy(rng.standard_normal((64, 128, 4)).astype(np.float32) * 0.1).to(DEV)
+        cv = torch.from_numpy(rng.standard_normal((64, 128, 4)).astype(np.float32)).to(DEV)
+        q = codec.synthesize_queries(1, 2, 32, seed=5, device=DEV).reshape(64, 128)
+        dense = codec.dequantize(enc, compensator_keys=ck, compensator_values=cv)
+        proj = codec.encoded_projection(enc, q, compensator_keys=ck, compensator_values=cv)
+        torch.cuda.synchronize()
+        args = (to_np(enc.codes), to_np(enc.smoothing), to_np(enc.scales))
+        assert_bit_exact(f"{layout} dense+comp", to_np(dense),
+                         oracle.dequantize(*args, to_np(ck), to_np(cv), layout=layout))
+        assert_close_and_exact(f"{layout} projection+comp", to_np(proj),
+                               oracle.project(*args, to_np(q.float()), to_np(ck), to_np(cv),
+                                              layout=layout))
