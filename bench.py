@@ -30,6 +30,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "gdn-state-codec_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))  # CPU-baseline leg only (the checker)
 
 METRIC = "codec HBM GB/s (% of B200 peak) and states/sec at 1/2/4/8 B200"
 UNIT = "states/s"
@@ -274,8 +275,11 @@ def main() -> None:
     barrier()
 
     if args.profile:
+        queries = codec.synthesize_queries(slots, LAYERS, HEADS, seed=1, device=device)
+        outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
         for _ in range(args.steps):
             step()
+            codec.encoded_projection(encoded, queries, out=outputs)
         barrier()
         if rank == 0:
             print(json.dumps({"profile": True, "heads": heads, "steps": args.steps}))
@@ -302,6 +306,23 @@ def main() -> None:
     deq_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in per_step)
     ms_per_step = elapsed_ms / args.steps
     value = world * heads * args.steps / (elapsed_ms / 1e3)
+
+    # ---- encoded projection over the same 30-layer cache (config 3 kernel) ----
+    queries = codec.synthesize_queries(slots, LAYERS, HEADS, seed=1, slot_base=rank * slots,
+                                       device=device)
+    outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
+    for _ in range(3):
+        codec.encoded_projection(encoded, queries, out=outputs)
+    barrier()
+    p_start = torch.cuda.Event(enable_timing=True)
+    p_end = torch.cuda.Event(enable_timing=True)
+    proj_iters = max(10, args.steps)
+    p_start.record(stream)
+    for _ in range(proj_iters):
+        codec.encoded_projection(encoded, queries, out=outputs)
+    p_end.record(stream)
+    barrier()
+    proj_ms = max_over_ranks(p_start.elapsed_time(p_end)) / proj_iters
 
     # ---- end to end through the public API with host buffers -----------------
     e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
@@ -330,7 +351,13 @@ def main() -> None:
             },
             "hbm_gbs_per_gpu": step_gbs,
             "hbm_frac_per_gpu": step_gbs / peak,
-            "kernels_ms": {"quantize": quant_ms, "dequantize": deq_ms},
+            "kernels": {
+                name: {"ms": ms, "gbs": BYTES_PER_HEAD[name] * heads / (ms / 1e3) / 1e9,
+                       "frac": BYTES_PER_HEAD[name] * heads / (ms / 1e3) / 1e9 / peak,
+                       "states_per_s": heads / (ms / 1e3)}
+                for name, ms in (("quantize", quant_ms), ("dequantize", deq_ms),
+                                 ("projection", proj_ms))
+            },
             "roofline": {
                 "bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                 "peak_kind": f"{peak_kind} (hbm_gbs, burst copy)", "unit": "GB/s",

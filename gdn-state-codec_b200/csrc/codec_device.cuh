@@ -69,6 +69,19 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
   return d;
 }
 
+// Separately rounded product destined for an add.  ptxas (CUDA 12.9) turns a
+// single-use mul.rn.f32x2 whose result feeds add.rn.f32x2 into one fused
+// multiply-add, despite the explicit rounding modifier and -fmad=false (found
+// by a GPU rounding check: every element where fma != mul-then-add followed
+// the fma).  An fma with a +0 addend is not contracted further and equals
+// RN(a * b), except that a -0 product comes out as +0.  Adding +0 instead of
+// -0 changes a sum only when the running sum is -0, and a round-to-nearest sum
+// that starts at +0 is never -0 (x + y = -0 needs x = y = -0), so every
+// accumulation below that starts at +0 is bit-identical to the reference's.
+__device__ __forceinline__ f2 mul2_for_add(f2 a, f2 b) {
+  return fma2(a, b, pack2(0.0F, 0.0F));
+}
+
 // --------------------------------------------------------------------------
 // int8 code <-> float without the conversion pipe.  For a word holding four
 // int8 codes, xor 0x80 turns each into the biased byte z + 128; placing that

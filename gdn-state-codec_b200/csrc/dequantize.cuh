@@ -59,23 +59,22 @@ __device__ __forceinline__ float4 dequant4(uint32_t word, f2 c01, f2 c23, f2 b01
   return make_float4(lo2(o01), hi2(o01), lo2(o23), hi2(o23));
 }
 
-// value += K[k][r] * V[v][r], r = 0..3 in order (capsule.cpp:241-246).
+// value += K[k][r] * V[v][r], r = 0..3 in order (capsule.cpp:241-246).  The
+// running value may be -0 for arbitrary caller data, so this (full-codec,
+// off the quant-only hot path) sum uses scalar .rn operations, which are never
+// contracted, rather than the packed +0-addend product of mul2_for_add.
 __device__ __forceinline__ float4 add_compensation(float4 d, const float4 kr[4], const float4 vr[4]) {
-  f2 d01 = pack2(d.x, d.y), d23 = pack2(d.z, d.w);
+  float out[4] = {d.x, d.y, d.z, d.w};
 #pragma unroll
   for (int r = 0; r < kRank; ++r) {
-    const float k0 = reinterpret_cast<const float*>(&kr[0])[r];
-    const float k1 = reinterpret_cast<const float*>(&kr[1])[r];
-    const float k2 = reinterpret_cast<const float*>(&kr[2])[r];
-    const float k3 = reinterpret_cast<const float*>(&kr[3])[r];
-    const float v0 = reinterpret_cast<const float*>(&vr[0])[r];
-    const float v1 = reinterpret_cast<const float*>(&vr[1])[r];
-    const float v2 = reinterpret_cast<const float*>(&vr[2])[r];
-    const float v3 = reinterpret_cast<const float*>(&vr[3])[r];
-    d01 = add2(d01, mul2(pack2(k0, k1), pack2(v0, v1)));
-    d23 = add2(d23, mul2(pack2(k2, k3), pack2(v2, v3)));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float k = reinterpret_cast<const float*>(&kr[i])[r];
+      const float v = reinterpret_cast<const float*>(&vr[i])[r];
+      out[i] = __fadd_rn(out[i], __fmul_rn(k, v));
+    }
   }
-  return make_float4(lo2(d01), hi2(d01), lo2(d23), hi2(d23));
+  return make_float4(out[0], out[1], out[2], out[3]);
 }
 
 template <bool kProvider, bool kCompensated>

@@ -55,8 +55,8 @@ __device__ __forceinline__ float4 bf16x4_to_float4(uint2 w) {
 // One k step for four outputs whose codes are given as magic floats.
 __device__ __forceinline__ void accumulate(f2& a01, f2& a23, f2 z01, f2 z23, float c, float x) {
   const f2 cc = pack2(c, c), xx = pack2(x, x);
-  a01 = add2(a01, mul2(mul2(z01, cc), xx));
-  a23 = add2(a23, mul2(mul2(z23, cc), xx));
+  a01 = add2(a01, mul2_for_add(mul2(z01, cc), xx));
+  a23 = add2(a23, mul2_for_add(mul2(z23, cc), xx));
 }
 
 __device__ __forceinline__ float4 finish_outputs(f2 a01, f2 a23, float4 b4, bool comp,
@@ -74,9 +74,10 @@ __device__ __forceinline__ float4 finish_outputs(f2 a01, f2 a23, float4 b4, bool
 #pragma unroll
     for (int i = 0; i < 4; ++i) q[i] = div127_any(rp[i]);
   }
+  // output = 0 + (rp / 127) * b (capsule.cpp:264, 288-289)
   const f2 zero = pack2(0.F, 0.F);
-  f2 o01 = add2(zero, mul2(pack2(q[0], q[1]), pack2(b4.x, b4.y)));
-  f2 o23 = add2(zero, mul2(pack2(q[2], q[3]), pack2(b4.z, b4.w)));
+  f2 o01 = add2(zero, mul2_for_add(pack2(q[0], q[1]), pack2(b4.x, b4.y)));
+  f2 o23 = add2(zero, mul2_for_add(pack2(q[2], q[3]), pack2(b4.z, b4.w)));
   if (comp) {
     const float p[4] = {lo2(kp01), hi2(kp01), lo2(kp23), hi2(kp23)};
     const float4 v0 = __ldg(reinterpret_cast<const float4*>(vbase) + 0);
@@ -90,8 +91,8 @@ __device__ __forceinline__ float4 finish_outputs(f2 a01, f2 a23, float4 b4, bool
       const float e1 = reinterpret_cast<const float*>(&v1)[r];
       const float e2 = reinterpret_cast<const float*>(&v2)[r];
       const float e3 = reinterpret_cast<const float*>(&v3)[r];
-      o01 = add2(o01, mul2(pack2(e0, e1), pp));
-      o23 = add2(o23, mul2(pack2(e2, e3), pp));
+      o01 = add2(o01, mul2_for_add(pack2(e0, e1), pp));
+      o23 = add2(o23, mul2_for_add(pack2(e2, e3), pp));
     }
   }
   return make_float4(lo2(o01), hi2(o01), lo2(o23), hi2(o23));
@@ -174,8 +175,8 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
           if (kCompensated) {
             const float4 kk = sh.kr[warp][k0 + i];
             const f2 xx = pack2(cx.y, cx.y);
-            kp01 = add2(kp01, mul2(pack2(kk.x, kk.y), xx));
-            kp23 = add2(kp23, mul2(pack2(kk.z, kk.w), xx));
+            kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
+            kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
           }
         }
       }
@@ -203,8 +204,8 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
             if (kCompensated) {
               const float4 kk = sh.kr[warp][k];
               const f2 xx = pack2(cx.y, cx.y);
-              kp01 = add2(kp01, mul2(pack2(kk.x, kk.y), xx));
-              kp23 = add2(kp23, mul2(pack2(kk.z, kk.w), xx));
+              kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
+              kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
             }
           }
         }
