@@ -16,6 +16,16 @@
 
 namespace gdnsc {
 
+// Test support: the quantizer's exact-division routine (div4_exact) applied
+// elementwise, so tests can compare it with IEEE division on the device.
+__global__ void division_selftest_kernel(const float* a, const float* c, float* out, uint64_t n) {
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const float ci = c[i];
+    out[i] = div4_exact_s(make_float4(a[i], 0.F, 0.F, 0.F), __frcp_rn(ci), -ci).x;
+  }
+}
+
 namespace {
 
 constexpr int32_t kOk = 0;
@@ -397,6 +407,19 @@ int32_t statecentric_gdn_state_codec_synthesize_queries_v1(void* stream, uint16_
                  cudaSuccess
              ? gdnsc::kOk
              : gdnsc::kLaunchFailed;
+}
+
+int32_t statecentric_gdn_state_codec_division_selftest_v1(void* stream, const float* numerators,
+                                                          const float* divisors, float* quotients,
+                                                          uint64_t count) {
+  if (numerators == nullptr || divisors == nullptr || quotients == nullptr || count == 0u) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::division_selftest_kernel<<<s->sms * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      numerators, divisors, quotients, count);
+  return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
 }
 
 // ---- Loader-compatibility entry points (windowed decode is not implemented) -----

@@ -13,18 +13,21 @@
 // Design (HBM-bound: 64 KiB read + 17 KiB written per head):
 //  * one persistent 512-thread CTA per SM with a ring of kStages 64 KiB
 //    shared-memory landing buffers, each filled by one TMA bulk copy
-//    (cp.async.bulk + mbarrier); while a head is computed from registers the
-//    next kStages-1 heads stream in.
-//  * warp w holds rows 8w..8w+7 of the head, lane l holds columns 4l..4l+3
-//    (32 floats per thread, read with conflict-free 128-bit shared loads: a
-//    warp reads one 512-byte row per instruction).
-//  * smoothing sums run in double; the per-value maximum and the codes run in
-//    fp32 from one multiply by RN(1/c) with a proven error bound, and the few
-//    elements inside that bound of a decision point are recomputed with IEEE
-//    division, so every output is exact.
-//  * capsule layout: row sums by warp shuffles, column maxima through shared
-//    memory; provider layout: column sums through shared memory, row maxima
-//    by warp shuffles.
+//    (cp.async.bulk + mbarrier).  A buffer stays valid while its head is
+//    processed (the rare exact paths read it by run-time index) and is
+//    refilled once every thread has moved on, so kStages - 1 heads are always
+//    in flight behind the one being computed.
+//  * the smoothing sums run in double (tree order, with a proof-backed check
+//    that sends the rare order-sensitive rows to the reference's sequential
+//    order); every smoothed value s = R / c is computed correctly rounded from
+//    RN(1/c) by two packed fma corrections (div4_exact), so the per-value
+//    maxima b are exact without any search; codes come from one multiply by
+//    RN(127 / b) and the few elements within the proven error band of a
+//    rounding boundary are recomputed with IEEE division.
+//  * thread tiles keep the double-precision reduction mostly inside a thread:
+//    capsule layout (row sums over values) uses 4 rows x 8 columns per thread,
+//    provider layout (column sums over values) 8 rows x 4 columns; both read
+//    the landing buffer without bank conflicts.
 #pragma once
 
 #include "codec_device.cuh"
@@ -32,23 +35,24 @@
 namespace gdnsc {
 
 constexpr int kQThreads = 512;
-constexpr int kQWarps = kQThreads / 32;        // 16
-constexpr int kRowsPerWarp = kKeys / kQWarps;  // 8
-constexpr int kLanesPerRow = 32 / kRowsPerWarp;  // 4 lanes share a reduced row
-constexpr int kStages = 2;
+constexpr int kQWarps = kQThreads / 32;      // 16
+constexpr int kWarpRows = kKeys / kQWarps;   // 8 rows of a head per warp
+constexpr int kStages = 3;                   // TMA landing buffers per CTA
 
-// Error bound of the reciprocal product: s' = RN(R * RN(1/c)) is within
-// 1.5 * 2^-23 of RN(R / c) relative (two roundings of 2^-24 each plus the
-// reciprocal's), so (a) the exact maximum can only come from an element whose
-// s' is within 2^-20 of the approximate maximum m', and (b) the approximate
-// scaled value t' = RN(s' * RN(127 / m')) is within 2^-13.7 of the exact
-// RN(RN(s / m) * 127): a code is decided directly unless t' lies within
-// 2^-12 of a rounding boundary n + 0.5.  Outside [2^-100, 2^100] (all-zero or
-// denormal columns, non-finite data) the exact path is taken for the column.
-constexpr float kCandidateFactor = 1.0F - 0x1p-20F;
-constexpr float kAmbiguous = 0.5F - 0x1p-12F;
-constexpr float kFastMin = 0x1p-100F;
+// Codes: t' = RN(s * RN(127 / b)) and the exact t = RN(RN(s / b) * 127) both
+// lie within 2^-23 (relative, two roundings each) of s * 127 / b, so
+// |t' - t| <= 127 * 2^-22 < 2^-15: a code is decided from t' unless t' lies
+// within 2^-13 of a rounding boundary n + 0.5.
+constexpr float kAmbiguous = 0.5F - 0x1p-13F;
+// Fast-path ranges: a per-value maximum b in [2^-64, 2^100] and smoothing in
+// [2^-14, 2^100] keep every element that can be a maximum or have a nonzero
+// code (|s| >= b / 254) inside div4_exact's preconditions (|R| >= 2^-102,
+// normal quotient).  Smoothing computed here is always >= sqrt(1e-8) = 1e-4.
+// Values outside (all-zero or denormal columns, non-finite data, caller-given
+// smoothing out of range) take the IEEE path for the affected columns.
+constexpr float kFastMin = 0x1p-64F;
 constexpr float kFastMax = 0x1p100F;
+constexpr float kSmoothMin = 0x1p-14F;
 
 enum QuantizeMode : int {
   kFused = 0,           // smoothing + quantize (initialize_launch_v3)
@@ -73,34 +77,26 @@ struct __align__(128) QuantizeShared {
     float col_part[kQWarps][kValues];  // capsule: per-warp column maxima
     double col_dsum[kQWarps][kKeys];   // provider: per-warp column sums
   };
-  float key_c[kKeys];            // provider: smoothing per key
-  float key_y[kKeys];            // provider: RN(1/c) per key
-  float col_km[kValues];         // capsule: RN(127 / m') per column
-  float col_thr[kValues];        // capsule: candidate threshold per column
-  uint32_t col_exact[kValues];   // capsule: exact column maximum (bits)
-  float colbuf[kKeys];           // provider: one column for a sequential re-sum
-  float row_c[kQWarps][kRowsPerWarp];       // capsule: smoothing of my rows
-  float row_y[kQWarps][kRowsPerWarp];       // capsule: RN(1/c) of my rows
-  float row_km[kQWarps][kRowsPerWarp];      // provider: per-row km
-  float row_thr[kQWarps][kRowsPerWarp];     // provider: per-row threshold
-  uint32_t row_exact[kQWarps][kRowsPerWarp];  // provider: exact row maximum
+  float key_c[kKeys];               // provider: smoothing per key
+  float key_y[kKeys];               // provider: RN(1/c) per key
+  float col_b[kValues];             // capsule: exact per-value maximum
+  float col_km[kValues];            // capsule: RN(127 / b) (0 on the IEEE path)
+  uint32_t col_exact[kValues];      // capsule IEEE path: maximum (bits)
+  float colbuf[kKeys];              // provider: one column for a sequential re-sum
+  float row_c[kQWarps][kWarpRows];  // capsule: smoothing of the warp's rows
+  float row_y[kQWarps][kWarpRows];  // capsule: RN(1/c) of the warp's rows
+  float row_b[kQWarps][kWarpRows];  // provider: exact per-value maximum
+  float row_km[kQWarps][kWarpRows]; // provider: RN(127 / b) (0 on the IEEE path)
   int col_flag[kKeys];
-  uint64_t full[kStages];        // one mbarrier per landing buffer
+  uint64_t full[kStages];           // one mbarrier per landing buffer
 };
 
 // ---------------------------------------------------------------------------
 // Small helpers.
 
-__device__ __forceinline__ float4 mul4s(float4 a, float y) {
-  const f2 yy = pack2(y, y);
-  const f2 lo = mul2(pack2(a.x, a.y), yy);
-  const f2 hi = mul2(pack2(a.z, a.w), yy);
-  return make_float4(lo2(lo), hi2(lo), lo2(hi), hi2(hi));
-}
-__device__ __forceinline__ float4 mul4v(float4 a, float4 y) {
-  const f2 lo = mul2(pack2(a.x, a.y), pack2(y.x, y.y));
-  const f2 hi = mul2(pack2(a.z, a.w), pack2(y.z, y.w));
-  return make_float4(lo2(lo), hi2(lo), lo2(hi), hi2(hi));
+__device__ __forceinline__ float4 absmax4v(float4 m, float4 a) {
+  return make_float4(fmaxf(m.x, fabsf(a.x)), fmaxf(m.y, fabsf(a.y)), fmaxf(m.z, fabsf(a.z)),
+                     fmaxf(m.w, fabsf(a.w)));
 }
 __device__ __forceinline__ float absmax4(float4 a) {
   return fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
@@ -108,10 +104,18 @@ __device__ __forceinline__ float absmax4(float4 a) {
 __device__ __forceinline__ float comp(const float4& a, int i) {
   return i == 0 ? a.x : (i == 1 ? a.y : (i == 2 ? a.z : a.w));
 }
+__device__ __forceinline__ double abs_sum4(float4 a) {
+  return (static_cast<double>(fabsf(a.x)) + static_cast<double>(fabsf(a.y))) +
+         (static_cast<double>(fabsf(a.z)) + static_cast<double>(fabsf(a.w)));
+}
+__device__ __forceinline__ bool fast_max(float b) { return b >= kFastMin && b <= kFastMax; }
+__device__ __forceinline__ bool fast_smoothing(float c) {
+  return c >= kSmoothMin && c <= kFastMax;
+}
 
-// Approximate codes for four elements: t = s * km rounded through the magic
-// constant; returns the packed int8x4 word and flags elements within the
-// ambiguity band of a rounding boundary.
+// Approximate codes of four elements from exact s: t = s * km rounded through
+// the magic constant; returns the packed int8x4 word and reports whether any
+// element lies within the ambiguity band of a rounding boundary.
 __device__ __forceinline__ uint32_t approx_codes(float4 s, float4 km, bool* amb) {
   const f2 t01 = mul2(pack2(s.x, s.y), pack2(km.x, km.y));
   const f2 t23 = mul2(pack2(s.z, s.w), pack2(km.z, km.w));
@@ -122,7 +126,7 @@ __device__ __forceinline__ uint32_t approx_codes(float4 s, float4 km, bool* amb)
   const f2 d23 = sub2(t23, sub2(u23, magic));
   const float worst = fmaxf(fmaxf(fabsf(lo2(d01)), fabsf(hi2(d01))),
                             fmaxf(fabsf(lo2(d23)), fabsf(hi2(d23))));
-  *amb = *amb || !(worst <= kAmbiguous);
+  *amb = !(worst <= kAmbiguous);
   const uint32_t w01 = __byte_perm(static_cast<uint32_t>(u01), static_cast<uint32_t>(u01 >> 32), 0x0040);
   const uint32_t w23 = __byte_perm(static_cast<uint32_t>(u23), static_cast<uint32_t>(u23 >> 32), 0x0040);
   return __byte_perm(w01, w23, 0x5410);
@@ -133,55 +137,6 @@ __device__ __forceinline__ bool approx_ambiguous(float s, float km) {
   const float u = __fadd_rn(t, kRoundMagic);
   const float d = __fsub_rn(t, __fsub_rn(u, kRoundMagic));
   return !(fabsf(d) <= kAmbiguous);
-}
-
-__device__ __forceinline__ float4 select_row(const float4 (&v)[kRowsPerWarp], int r) {
-  float4 out = v[0];
-#pragma unroll
-  for (int j = 1; j < kRowsPerWarp; ++j) {
-    if (j == r) out = v[j];
-  }
-  return out;
-}
-
-// Warp reduce-scatter of kRowsPerWarp per-row partials: afterwards the
-// kLanesPerRow lanes with lane / kLanesPerRow == r hold the total of row r.
-__device__ __forceinline__ double reduce_scatter_sum(double (&p)[kRowsPerWarp], int lane) {
-  int offset = 16;
-#pragma unroll
-  for (int half = kRowsPerWarp / 2; half >= 1; half >>= 1, offset >>= 1) {
-    const bool upper = (lane & offset) != 0;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const double send = upper ? p[i] : p[i + half];
-      const double keep = upper ? p[i + half] : p[i];
-      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, offset);
-    }
-  }
-  double total = p[0];
-#pragma unroll
-  for (int o = kLanesPerRow / 2; o >= 1; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-  return total;
-}
-
-__device__ __forceinline__ float reduce_scatter_max(float (&p)[kRowsPerWarp], int lane) {
-  int offset = 16;
-#pragma unroll
-  for (int half = kRowsPerWarp / 2; half >= 1; half >>= 1, offset >>= 1) {
-    const bool upper = (lane & offset) != 0;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const float send = upper ? p[i] : p[i + half];
-      const float keep = upper ? p[i + half] : p[i];
-      p[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, offset));
-    }
-  }
-  float total = p[0];
-#pragma unroll
-  for (int o = kLanesPerRow / 2; o >= 1; o >>= 1) {
-    total = fmaxf(total, __shfl_xor_sync(0xffffffffu, total, o));
-  }
-  return total;
 }
 
 // Next work item at or after `item` (stride `step`) that names a real head.
@@ -201,49 +156,87 @@ __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t 
   return item;
 }
 
-__device__ __forceinline__ void issue_head(QuantizeShared& sh, const QuantizeParams& p, int stage,
+__device__ __forceinline__ void issue_head(const QuantizeParams& p, float* buffer, uint64_t* bar,
                                            int64_t head) {
   fence_proxy_async();
-  mbar_expect_tx(&sh.full[stage], kElements * sizeof(float));
-  bulk_load(sh.stage[stage], p.state + static_cast<uint64_t>(head) * kElements,
-            kElements * sizeof(float), &sh.full[stage], evict_first_policy());
+  mbar_expect_tx(bar, kElements * sizeof(float));
+  bulk_load(buffer, p.state + static_cast<uint64_t>(head) * kElements, kElements * sizeof(float),
+            bar, evict_first_policy());
 }
 
 // ---------------------------------------------------------------------------
-// Capsule layout [key, value]: row k = key, column v = value.  Returns false
-// when the block must stop (a bounded wait expired somewhere in the block).
+// Capsule layout [key, value]: row k = key, column v = value.
+//
+// Thread tile: lane l = 16g + q (g = l/16, q = l%16) of warp w holds rows
+// r_j = 8w + 2j + g (j = 0..3) and, in each row, two 4-column chunks c = 0, 1
+// at columns 64c + 4q .. 64c + 4q + 3.  For a fixed (j, c) a half warp reads
+// 256 contiguous bytes of one row: conflict-free.  A row is shared by the 16
+// lanes of one g (row sums reduce over lane bits 0-3); a column by the two
+// lanes of one q (column maxima reduce over lane bit 4, then across warps).
+
+struct CapsuleTile {
+  float4 v[4][2];  // [row j][chunk c]: R, then s = R / c
+};
+
+__device__ __forceinline__ void load_capsule_tile(const float* stage_f, CapsuleTile& t, int warp,
+                                                  int lane) {
+  const int g = lane >> 4, q = lane & 15;
+  const float4* stage = reinterpret_cast<const float4*>(stage_f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int row = warp * kWarpRows + 2 * j + g;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) t.v[j][c] = stage[row * 32 + 16 * c + q];
+  }
+}
 
 template <int kMode>
-__device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p, QuantizeShared& sh,
-                                                      const float4 (&v)[kRowsPerWarp],
-                                                      int64_t head, int warp, int lane, int tid,
-                                                      bool timed_out, int stage,
-                                                      int64_t refill_head) {
-  const int row0 = warp * kRowsPerWarp;
-  // -- smoothing per row (warp-local) -----------------------------------------
+__device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p, QuantizeShared& sh,
+                                                      CapsuleTile& t, const float* stage,
+                                                      int64_t head, int warp, int lane, int tid) {
+  const int g = lane >> 4, q = lane & 15;
+  const int row_base = warp * kWarpRows;
+  // -- smoothing per row -----------------------------------------------------
+  bool bad_smoothing = false;
   if (kMode == kGivenSmoothing) {
-    if (lane < kRowsPerWarp) {
-      const float c = __ldg(p.smoothing_in + head * kKeys + row0 + lane);
+    if (lane < kWarpRows) {
+      const float c = __ldg(p.smoothing_in + head * kKeys + row_base + lane);
       sh.row_c[warp][lane] = c;
       sh.row_y[warp][lane] = __frcp_rn(c);
+      bad_smoothing = !fast_smoothing(c);
     }
   } else {
-    double part[kRowsPerWarp];
+    double part[4];
 #pragma unroll
-    for (int j = 0; j < kRowsPerWarp; ++j) {
-      part[j] = (static_cast<double>(fabsf(v[j].x)) + static_cast<double>(fabsf(v[j].y))) +
-                (static_cast<double>(fabsf(v[j].z)) + static_cast<double>(fabsf(v[j].w)));
+    for (int j = 0; j < 4; ++j) part[j] = abs_sum4(t.v[j][0]) + abs_sum4(t.v[j][1]);
+    // Reduce-scatter over the 16 lanes of this g (lane bits 3, 2), then sum
+    // over lane bits 1, 0: lanes 4i..4i+3 of the half warp hold row j = i.
+    {
+      const bool up = (lane & 8) != 0;
+      const double s0 = up ? part[0] : part[2], s1 = up ? part[1] : part[3];
+      const double k0 = up ? part[2] : part[0], k1 = up ? part[3] : part[1];
+      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 8);
+      part[1] = k1 + __shfl_xor_sync(0xffffffffu, s1, 8);
     }
-    double sum = reduce_scatter_sum(part, lane);
-    const int my_row = lane / kLanesPerRow;
+    {
+      const bool up = (lane & 4) != 0;
+      const double s0 = up ? part[0] : part[1];
+      const double k0 = up ? part[1] : part[0];
+      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 4);
+    }
+    double sum = part[0] + __shfl_xor_sync(0xffffffffu, part[0], 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    const int my_j = (lane >> 2) & 3;  // this lane group's row r = 8w + 2*my_j + g
     // Rows whose float mean could depend on the summation order are re-summed
-    // in the reference's order (capsule.cpp:193-196): value 0..127.
-    uint32_t flagged = __ballot_sync(0xffffffffu, near_float_midpoint(sum * (1.0 / 128.0))) &
-                       0x11111111u;
+    // in the reference's order (capsule.cpp:193-196): value 0..127, read from
+    // the landing buffer.  Rare.
+    uint32_t flagged =
+        __ballot_sync(0xffffffffu, near_float_midpoint(sum * (1.0 / 128.0))) & 0x11111111u;
     while (flagged != 0u) {
       const int owner = __ffs(flagged) - 1;
       flagged &= flagged - 1u;
-      const float4 mine = select_row(v, owner / kLanesPerRow);
+      const int row = row_base + 2 * ((owner >> 2) & 3) + (owner >> 4);
+      const float4 mine = reinterpret_cast<const float4*>(stage)[row * 32 + lane];
       double seq = 0.0;
       for (int src = 0; src < 32; ++src) {
         seq += fabsf(__shfl_sync(0xffffffffu, mine.x, src));
@@ -251,115 +244,142 @@ __device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p, Q
         seq += fabsf(__shfl_sync(0xffffffffu, mine.z, src));
         seq += fabsf(__shfl_sync(0xffffffffu, mine.w, src));
       }
-      if (my_row == owner / kLanesPerRow) sum = seq;
+      if ((lane >> 2) == (owner >> 2)) sum = seq;
     }
     const float c = smoothing_from_sum(sum);
-    if (lane % kLanesPerRow == 0) {
-      sh.row_c[warp][my_row] = c;
-      sh.row_y[warp][my_row] = __frcp_rn(c);
-      p.smoothing[head * kKeys + row0 + my_row] = c;
+    if ((lane & 3) == 0) {
+      const int r = 2 * my_j + g;
+      sh.row_c[warp][r] = c;
+      sh.row_y[warp][r] = __frcp_rn(c);
+      p.smoothing[head * kKeys + row_base + r] = c;
     }
   }
   __syncwarp();
-  if (kMode == kSmoothingOnly) {
-    if (__syncthreads_or(timed_out) != 0) return false;
-    if (tid == 0 && refill_head >= 0) issue_head(sh, p, stage, refill_head);
-    return true;
-  }
+  if (kMode == kSmoothingOnly) return;
 
-  // -- approximate column maxima -------------------------------------------
-  float4 pm = make_float4(0.F, 0.F, 0.F, 0.F);
+  // -- exact smoothed values and column maxima ------------------------------------
+  float4 pm[2] = {make_float4(0.F, 0.F, 0.F, 0.F), make_float4(0.F, 0.F, 0.F, 0.F)};
 #pragma unroll
-  for (int j = 0; j < kRowsPerWarp; ++j) {
-    const float4 s = mul4s(v[j], sh.row_y[warp][j]);
-    pm.x = fmaxf(pm.x, fabsf(s.x));
-    pm.y = fmaxf(pm.y, fabsf(s.y));
-    pm.z = fmaxf(pm.z, fabsf(s.z));
-    pm.w = fmaxf(pm.w, fabsf(s.w));
+  for (int j = 0; j < 4; ++j) {
+    const float y = sh.row_y[warp][2 * j + g];
+    const float nc = -sh.row_c[warp][2 * j + g];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      t.v[j][c] = div4_exact_s(t.v[j][c], y, nc);
+      pm[c] = absmax4v(pm[c], t.v[j][c]);
+    }
   }
-  reinterpret_cast<float4*>(sh.col_part[warp])[lane] = pm;
-  // B1: every warp has read the landing buffer and published its maxima.
-  if (__syncthreads_or(timed_out) != 0) return false;
-  if (tid == 0 && refill_head >= 0) issue_head(sh, p, stage, refill_head);
+  {
+    // Exchange over lane bit 4: afterwards this lane holds the warp maximum
+    // of chunk c = g (columns 64g + 4q ..).
+    const bool up = (lane & 16) != 0;
+    const float4 send = up ? pm[0] : pm[1];
+    const float4 keep = up ? pm[1] : pm[0];
+    const float4 m = make_float4(fmaxf(keep.x, __shfl_xor_sync(0xffffffffu, send.x, 16)),
+                                 fmaxf(keep.y, __shfl_xor_sync(0xffffffffu, send.y, 16)),
+                                 fmaxf(keep.z, __shfl_xor_sync(0xffffffffu, send.z, 16)),
+                                 fmaxf(keep.w, __shfl_xor_sync(0xffffffffu, send.w, 16)));
+    reinterpret_cast<float4*>(sh.col_part[warp])[16 * g + q] = m;
+  }
+  const bool head_slow = __syncthreads_or(bad_smoothing) != 0;  // B1
   int slow = 0;
   if (tid < kValues) {
-    float m = 0.0F;
+    float b = 0.0F;
 #pragma unroll
-    for (int w = 0; w < kQWarps; ++w) m = fmaxf(m, sh.col_part[w][tid]);
-    slow = !(m >= kFastMin && m <= kFastMax);
-    sh.col_km[tid] = slow ? 0.0F : __fdiv_rn(kQuantMax, m);
-    sh.col_thr[tid] = slow ? -1.0F : __fmul_rn(m, kCandidateFactor);
+    for (int w = 0; w < kQWarps; ++w) b = fmaxf(b, sh.col_part[w][tid]);
+    slow = head_slow || !fast_max(b);
+    sh.col_b[tid] = b;
+    sh.col_km[tid] = slow ? 0.0F : __fdiv_rn(kQuantMax, b);
     sh.col_exact[tid] = 0u;
+    if (!slow) p.scales[head * kValues + tid] = b;
   }
   const bool any_slow = __syncthreads_or(slow) != 0;  // B2
 
-  // -- codes, and exact maxima from the candidates --------------------------
-  const float4 km = reinterpret_cast<const float4*>(sh.col_km)[lane];
-  const float4 thr = reinterpret_cast<const float4*>(sh.col_thr)[lane];
-  uint32_t amb_rows = 0u;
+  // -- codes ----------------------------------------------------------------------
+  uint32_t amb_mask = 0u;  // bit 2j+c: chunk (j, c) holds an ambiguous element
   int8_t* codes = p.codes + static_cast<uint64_t>(head) * kElements;
 #pragma unroll
-  for (int j = 0; j < kRowsPerWarp; ++j) {
-    const float4 s = mul4s(v[j], sh.row_y[warp][j]);
-    const bool cand = (fabsf(s.x) >= thr.x) || (fabsf(s.y) >= thr.y) ||
-                      (fabsf(s.z) >= thr.z) || (fabsf(s.w) >= thr.w);
-    if (cand) {
-      const float c = sh.row_c[warp][j];
+  for (int c = 0; c < 2; ++c) {
+    const float4 km = reinterpret_cast<const float4*>(sh.col_km)[16 * c + q];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float r = comp(v[j], i);
-        if (fabsf(comp(s, i)) >= comp(thr, i) && r != 0.0F) {
-          const float exact = fabsf(__fdiv_rn(r, c));
-          atomicMax(&sh.col_exact[4 * lane + i], __float_as_uint(exact));
+    for (int j = 0; j < 4; ++j) {
+      bool amb;
+      const uint32_t word = approx_codes(t.v[j][c], km, &amb);
+      st_cs_u32(codes + (row_base + 2 * j + g) * kValues + 64 * c + 4 * q, word);
+      amb_mask |= (amb ? 1u : 0u) << (2 * j + c);
+    }
+  }
+  // Elements inside the ambiguity band take the exact code (IEEE division
+  // from the landing buffer, exact maximum).
+  while (amb_mask != 0u) {
+    const int bit = __ffs(amb_mask) - 1;
+    amb_mask &= amb_mask - 1u;
+    const int r_local = 2 * (bit >> 1) + g, c = bit & 1;
+    const float c_r = sh.row_c[warp][r_local];
+    const float y_r = sh.row_y[warp][r_local];
+    for (int e = 0; e < 4; ++e) {
+      const int col = 64 * c + 4 * q + e;
+      const float km = sh.col_km[col];
+      if (km == 0.0F) continue;  // IEEE-path column, handled below
+      const float r = stage[(row_base + r_local) * kValues + col];
+      if (approx_ambiguous(div4_exact_s(make_float4(r, 0.F, 0.F, 0.F), y_r, -c_r).x, km)) {
+        codes[(row_base + r_local) * kValues + col] = exact_code(__fdiv_rn(r, c_r), sh.col_b[col]);
+      }
+    }
+  }
+  if (any_slow) {
+    // IEEE path for columns outside the fast ranges (rare; all-zero columns
+    // included): exact quotients, an exact maximum across the block, codes.
+    for (int j = 0; j < 4; ++j) {
+      const int r_local = 2 * j + g;
+      for (int c = 0; c < 2; ++c) {
+        for (int e = 0; e < 4; ++e) {
+          const int col = 64 * c + 4 * q + e;
+          if (sh.col_km[col] != 0.0F) continue;
+          const float r = stage[(row_base + r_local) * kValues + col];
+          if (r != 0.0F) {
+            atomicMax(&sh.col_exact[col],
+                      __float_as_uint(fabsf(__fdiv_rn(r, sh.row_c[warp][r_local]))));
+          }
         }
       }
     }
-    bool amb = false;
-    const uint32_t word = approx_codes(s, km, &amb);
-    st_cs_u32(codes + (row0 + j) * kValues + 4 * lane, word);
-    amb_rows |= amb ? (1u << j) : 0u;
-  }
-  __syncthreads();  // B3: exact maxima complete
-  if (tid < kValues) p.scales[head * kValues + tid] = __uint_as_float(sh.col_exact[tid]);
-  // Elements inside the ambiguity band, and every element of a column outside
-  // the fast range, take the exact computation with the exact maximum.
-  const bool my_slow = any_slow && (thr.x < 0.F || thr.y < 0.F || thr.z < 0.F || thr.w < 0.F);
-  if (amb_rows != 0u || my_slow) {
-    for (int j = 0; j < kRowsPerWarp; ++j) {
-      const bool row_amb = (amb_rows >> j) & 1u;
-      if (!row_amb && !my_slow) continue;
-      const float4 r4 = select_row(v, j);
-      const float c = sh.row_c[warp][j];
-      const float yy = sh.row_y[warp][j];
-      for (int i = 0; i < 4; ++i) {
-        const int col = 4 * lane + i;
-        const float r = comp(r4, i);
-        bool redo = comp(thr, i) < 0.F;
-        if (!redo && row_amb) redo = approx_ambiguous(__fmul_rn(r, yy), comp(km, i));
-        if (!redo) continue;
-        const float m = __uint_as_float(sh.col_exact[col]);
-        codes[(row0 + j) * kValues + col] = exact_code(__fdiv_rn(r, c), m);
+    __syncthreads();
+    if (tid < kValues && sh.col_km[tid] == 0.0F) {
+      p.scales[head * kValues + tid] = __uint_as_float(sh.col_exact[tid]);
+    }
+    for (int j = 0; j < 4; ++j) {
+      const int r_local = 2 * j + g;
+      for (int c = 0; c < 2; ++c) {
+        for (int e = 0; e < 4; ++e) {
+          const int col = 64 * c + 4 * q + e;
+          if (sh.col_km[col] != 0.0F) continue;
+          const float r = stage[(row_base + r_local) * kValues + col];
+          codes[(row_base + r_local) * kValues + col] =
+              exact_code(r == 0.0F ? 0.0F : __fdiv_rn(r, sh.row_c[warp][r_local]),
+                         __uint_as_float(sh.col_exact[col]));
+        }
       }
     }
   }
-  return true;
 }
 
 // ---------------------------------------------------------------------------
 // Provider layout [value, key]: row = value v, column = key k.
+// Thread tile: warp w holds rows 8w..8w+7, lane l columns 4l..4l+3 (a warp
+// reads one 512-byte row per instruction: conflict-free).
 
 template <int kMode>
-__device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p, QuantizeShared& sh,
-                                                       const float4 (&v)[kRowsPerWarp],
-                                                       int64_t head, int warp, int lane, int tid,
-                                                       bool timed_out, int stage,
-                                                       int64_t refill_head) {
-  const int row0 = warp * kRowsPerWarp;
-  // -- smoothing per key (column), across warps --------------------------------
+__device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, QuantizeShared& sh,
+                                                       float4 (&v)[kWarpRows], const float* stage,
+                                                       int64_t head, int warp, int lane,
+                                                       int tid) {
+  const int row_base = warp * kWarpRows;
+  // -- smoothing per key (column): thread-local over 8 rows, then across warps
   if (kMode != kGivenSmoothing) {
     double cs0 = 0.0, cs1 = 0.0, cs2 = 0.0, cs3 = 0.0;
 #pragma unroll
-    for (int j = 0; j < kRowsPerWarp; ++j) {
+    for (int j = 0; j < kWarpRows; ++j) {
       cs0 += fabsf(v[j].x);
       cs1 += fabsf(v[j].y);
       cs2 += fabsf(v[j].z);
@@ -371,14 +391,14 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p, 
     dst[2] = cs2;
     dst[3] = cs3;
   }
-  // B1: every warp has read the landing buffer.
-  if (__syncthreads_or(timed_out) != 0) return false;
-  if (tid == 0 && refill_head >= 0) issue_head(sh, p, stage, refill_head);
+  __syncthreads();  // B1: column partial sums published
   int flag = 0;
+  bool bad_smoothing = false;
   if (tid < kKeys) {
     float c;
     if (kMode == kGivenSmoothing) {
       c = __ldg(p.smoothing_in + head * kKeys + tid);
+      bad_smoothing = !fast_smoothing(c);
     } else {
       double sum = 0.0;
 #pragma unroll
@@ -391,13 +411,13 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p, 
     sh.key_y[tid] = __frcp_rn(c);
     sh.col_flag[tid] = flag;
   }
-  if (__syncthreads_or(flag) != 0) {  // B2; the rare re-sum branch is block-uniform
+  // B2: smoothing ready; bit 0 = a column needs the sequential re-sum,
+  // bit 1 = caller-given smoothing outside the fast range.
+  const int b2 = __syncthreads_or(flag | (bad_smoothing ? 2 : 0));
+  if (b2 & 1) {  // rare, block-uniform
     for (int k = 0; k < kKeys; ++k) {
       if (!sh.col_flag[k]) continue;
-      if (lane == (k >> 2)) {
-#pragma unroll
-        for (int j = 0; j < kRowsPerWarp; ++j) sh.colbuf[row0 + j] = comp(v[j], k & 3);
-      }
+      if (tid < kValues) sh.colbuf[tid] = stage[tid * kKeys + k];
       __syncthreads();
       if (tid == 0) {
         double seq = 0.0;  // capsule.cpp:193-196 order: value 0..127
@@ -410,69 +430,91 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p, 
       __syncthreads();
     }
   }
-  if (kMode == kSmoothingOnly) return true;
+  if (kMode == kSmoothingOnly) return;
+  const bool head_slow = (b2 & 2) != 0;
 
+  // -- exact smoothed values and row maxima (warp-local) ------------------------------
+  const float4 c4 = reinterpret_cast<const float4*>(sh.key_c)[lane];
   const float4 y4 = reinterpret_cast<const float4*>(sh.key_y)[lane];
-  // -- approximate row maxima (warp-local) ---------------------------------------
-  float rm[kRowsPerWarp];
+  const float4 nc4 = make_float4(-c4.x, -c4.y, -c4.z, -c4.w);
+  float rm[kWarpRows];
 #pragma unroll
-  for (int j = 0; j < kRowsPerWarp; ++j) rm[j] = absmax4(mul4v(v[j], y4));
-  const float m = reduce_scatter_max(rm, lane);
-  if (lane % kLanesPerRow == 0) {
-    const int r = lane / kLanesPerRow;
-    const bool slow = !(m >= kFastMin && m <= kFastMax);
-    sh.row_km[warp][r] = slow ? 0.0F : __fdiv_rn(kQuantMax, m);
-    sh.row_thr[warp][r] = slow ? -1.0F : __fmul_rn(m, kCandidateFactor);
-    sh.row_exact[warp][r] = 0u;
+  for (int j = 0; j < kWarpRows; ++j) {
+    v[j] = div4_exact(v[j], y4, nc4);
+    rm[j] = absmax4(v[j]);
   }
+  {
+    int offset = 16;
+#pragma unroll
+    for (int half = kWarpRows / 2; half >= 1; half >>= 1, offset >>= 1) {
+      const bool up = (lane & offset) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? rm[i] : rm[i + half];
+        const float keep = up ? rm[i + half] : rm[i];
+        rm[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, offset));
+      }
+    }
+  }
+  float b = fmaxf(rm[0], __shfl_xor_sync(0xffffffffu, rm[0], 2));
+  b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 1));
+  const int my_row = lane >> 2;  // lanes 4r..4r+3 hold row r
+  const bool my_slow = head_slow || !fast_max(b);
+  if ((lane & 3) == 0) {
+    sh.row_b[warp][my_row] = b;
+    sh.row_km[warp][my_row] = my_slow ? 0.0F : __fdiv_rn(kQuantMax, b);
+    if (!my_slow) p.scales[head * kValues + row_base + my_row] = b;
+  }
+  const uint32_t slow_rows = __ballot_sync(0xffffffffu, my_slow && (lane & 3) == 0);
   __syncwarp();
 
-  // -- codes, and exact maxima from the candidates ---------------------------------
-  const float4 c4 = reinterpret_cast<const float4*>(sh.key_c)[lane];
-  uint32_t amb_rows = 0u, slow_rows = 0u;
+  // -- codes ------------------------------------------------------------------------
+  uint32_t amb_rows = 0u;
   int8_t* codes = p.codes + static_cast<uint64_t>(head) * kElements;
 #pragma unroll
-  for (int j = 0; j < kRowsPerWarp; ++j) {
+  for (int j = 0; j < kWarpRows; ++j) {
     const float km = sh.row_km[warp][j];
-    const float thr = sh.row_thr[warp][j];
-    const float4 s = mul4v(v[j], y4);
-    if (absmax4(s) >= thr) {
+    bool amb;
+    const uint32_t word = approx_codes(v[j], make_float4(km, km, km, km), &amb);
+    st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
+    amb_rows |= (amb ? 1u : 0u) << j;
+  }
+  while (amb_rows != 0u) {
+    const int j = __ffs(amb_rows) - 1;
+    amb_rows &= amb_rows - 1u;
+    const float km = sh.row_km[warp][j];
+    if (km == 0.0F) continue;  // IEEE-path row, handled below
+    const float4 r4 = reinterpret_cast<const float4*>(stage)[(row_base + j) * 32 + lane];
+    const float4 s4 = div4_exact(r4, y4, nc4);
+    for (int i = 0; i < 4; ++i) {
+      if (approx_ambiguous(comp(s4, i), km)) {
+        codes[(row_base + j) * kKeys + 4 * lane + i] =
+            exact_code(__fdiv_rn(comp(r4, i), comp(c4, i)), sh.row_b[warp][j]);
+      }
+    }
+  }
+  // IEEE path for rows outside the fast ranges (rare; all-zero rows included).
+  uint32_t slow_left = slow_rows;
+  while (slow_left != 0u) {
+    const int owner = __ffs(slow_left) - 1;
+    slow_left &= slow_left - 1u;
+    const int j = owner >> 2;
+    const float4 r4 = reinterpret_cast<const float4*>(stage)[(row_base + j) * 32 + lane];
+    float4 s4;
+    s4.x = r4.x == 0.0F ? 0.0F : __fdiv_rn(r4.x, c4.x);
+    s4.y = r4.y == 0.0F ? 0.0F : __fdiv_rn(r4.y, c4.y);
+    s4.z = r4.z == 0.0F ? 0.0F : __fdiv_rn(r4.z, c4.z);
+    s4.w = r4.w == 0.0F ? 0.0F : __fdiv_rn(r4.w, c4.w);
+    float mx = absmax4(s4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float r = comp(v[j], i);
-        if (fabsf(comp(s, i)) >= thr && r != 0.0F) {
-          const float exact = fabsf(__fdiv_rn(r, comp(c4, i)));
-          atomicMax(&sh.row_exact[warp][j], __float_as_uint(exact));
-        }
-      }
-    }
-    bool amb = false;
-    const uint32_t word = approx_codes(s, make_float4(km, km, km, km), &amb);
-    st_cs_u32(codes + (row0 + j) * kKeys + 4 * lane, word);
-    amb_rows |= amb ? (1u << j) : 0u;
-    slow_rows |= thr < 0.F ? (1u << j) : 0u;
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) p.scales[head * kValues + row_base + j] = mx;
+    const uint32_t word = (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.x, mx)))) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.y, mx))) << 8) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.z, mx))) << 16) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.w, mx))) << 24);
+    st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
   }
-  __syncwarp();
-  if (lane < kRowsPerWarp) {
-    p.scales[head * kValues + row0 + lane] = __uint_as_float(sh.row_exact[warp][lane]);
-  }
-  const uint32_t redo_rows = amb_rows | slow_rows;
-  if (redo_rows != 0u) {
-    for (int j = 0; j < kRowsPerWarp; ++j) {
-      if (!((redo_rows >> j) & 1u)) continue;
-      const float4 r4 = select_row(v, j);
-      const float km = sh.row_km[warp][j];
-      const float mx = __uint_as_float(sh.row_exact[warp][j]);
-      const bool row_slow = (slow_rows >> j) & 1u;
-      for (int i = 0; i < 4; ++i) {
-        const float r = comp(r4, i);
-        const bool redo = row_slow || approx_ambiguous(__fmul_rn(r, comp(y4, i)), km);
-        if (!redo) continue;
-        codes[(row0 + j) * kKeys + 4 * lane + i] = exact_code(__fdiv_rn(r, comp(c4, i)), mx);
-      }
-    }
-  }
-  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -493,13 +535,15 @@ __global__ void __launch_bounds__(kQThreads, 1) quantize_kernel(QuantizeParams p
   __syncthreads();
 
   // The producer (thread 0) runs kStages valid heads ahead of the consumers;
-  // both walk the same deterministic item sequence.
+  // both walk the same deterministic item sequence.  Head number n lives in
+  // landing buffer n % kStages, whose fill for it has parity (n / kStages) & 1.
   int64_t prod_head = -1;
-  uint64_t prod_item = next_item(p, blockIdx.x, step, &prod_head, false);
-  uint32_t issued = 0;  // loads issued so far (thread 0)
+  uint64_t prod_item = 0;
+  uint32_t issued = 0;
   if (tid == 0) {
+    prod_item = next_item(p, blockIdx.x, step, &prod_head, false);
     for (int s = 0; s < kStages && prod_head >= 0; ++s) {
-      issue_head(sh, p, s, prod_head);
+      issue_head(p, sh.stage[s], &sh.full[s], prod_head);
       ++issued;
       prod_item = next_item(p, prod_item + step, step, &prod_head, false);
     }
@@ -509,42 +553,42 @@ __global__ void __launch_bounds__(kQThreads, 1) quantize_kernel(QuantizeParams p
   uint32_t consumed = 0;
   while (head >= 0) {
     const int stage = static_cast<int>(consumed % kStages);
-    const uint32_t parity = (consumed / kStages) & 1u;
-    const bool timed_out = !mbar_wait_bounded(&sh.full[stage], parity);
-    float4 v[kRowsPerWarp];
-    const float4* src = reinterpret_cast<const float4*>(sh.stage[stage]);
+    const bool timed_out = !mbar_wait_bounded(&sh.full[stage], (consumed / kStages) & 1u);
+    CapsuleTile ct;
+    float4 pv[kWarpRows];
+    if (kProvider) {
+      const float4* src = reinterpret_cast<const float4*>(sh.stage[stage]);
 #pragma unroll
-    for (int j = 0; j < kRowsPerWarp; ++j) v[j] = src[(warp * kRowsPerWarp + j) * 32 + lane];
-    ++consumed;
-
-    // Head to stream into this landing buffer once every warp has read it.
-    int64_t refill = -1;
-    if (tid == 0) {
-      refill = prod_head;
-      if (prod_head >= 0) {
-        ++issued;
-        prod_item = next_item(p, prod_item + step, step, &prod_head, false);
-      }
+      for (int j = 0; j < kWarpRows; ++j) pv[j] = src[(warp * kWarpRows + j) * 32 + lane];
+    } else {
+      load_capsule_tile(sh.stage[stage], ct, warp, lane);
     }
-    const bool keep_going =
-        kProvider ? quantize_provider_head<kMode>(p, sh, v, head, warp, lane, tid, timed_out,
-                                                  stage, refill)
-                  : quantize_capsule_head<kMode>(p, sh, v, head, warp, lane, tid, timed_out,
-                                                 stage, refill);
-    if (!keep_going) {
-      // A bounded wait expired somewhere in the block (the head functions stop
-      // before issuing `refill`).  Report it, then wait, again bounded, for
-      // every copy that may still be in flight -- load indices consumed-1 up
-      // to the last one issued -- so none lands in this block's shared memory
-      // after it exits.  Outputs of this launch are then unspecified.
+    ++consumed;
+    // B0: every warp holds its part of this head and has finished the previous
+    // one, whose landing buffer now takes the head kStages - 1 ahead.
+    if (__syncthreads_or(timed_out) != 0) {
+      // A bounded wait expired: report it, then wait, again bounded, for every
+      // copy that may still be in flight (fills consumed-1 .. issued-1) so that
+      // none lands in this block's shared memory after it exits.  Outputs of
+      // this launch are then unspecified.
       if (tid == 0) {
         report(p.status, kStatusWaitTimeout);
-        const uint32_t issued_for_real = issued - (refill >= 0 ? 1u : 0u);
-        for (uint32_t idx = consumed - 1u; idx < issued_for_real; ++idx) {
-          (void)mbar_wait_bounded(&sh.full[idx % kStages], (idx / kStages) & 1u);
+        for (uint32_t n = consumed - 1u; n < issued; ++n) {
+          (void)mbar_wait_bounded(&sh.full[n % kStages], (n / kStages) & 1u);
         }
       }
       return;
+    }
+    if (tid == 0 && consumed >= 2 && prod_head >= 0) {
+      const int prev = static_cast<int>((consumed - 2) % kStages);
+      issue_head(p, sh.stage[prev], &sh.full[prev], prod_head);
+      ++issued;
+      prod_item = next_item(p, prod_item + step, step, &prod_head, false);
+    }
+    if (kProvider) {
+      quantize_provider_head<kMode>(p, sh, pv, sh.stage[stage], head, warp, lane, tid);
+    } else {
+      quantize_capsule_head<kMode>(p, sh, ct, sh.stage[stage], head, warp, lane, tid);
     }
     item = next_item(p, item + step, step, &head, tid == 0);
   }

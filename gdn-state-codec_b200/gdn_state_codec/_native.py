@@ -50,6 +50,7 @@ SIGNATURES: dict[str, list] = {
         [_vp, _vp, _u32, _u64, _u32, _u32, _u32, _u32],
     "statecentric_gdn_state_codec_synthesize_queries_v1":
         [_vp, _vp, _u64, _u32, _u32, _u32, _u32],
+    "statecentric_gdn_state_codec_division_selftest_v1": [_vp, _vp, _vp, _vp, _u64],
     # loader-compatibility entry points (windowed decode not implemented)
     "statecentric_gdn_state_codec_windowed_gdn_step_launch_v1": [_vp] * 16 + [_u32],
     "statecentric_gdn_state_codec_window_boundary_launch_v1": [_vp] * 16 + [_u32, _u32],

@@ -185,6 +185,15 @@ int32_t statecentric_gdn_state_codec_synthesize_queries_v1(
     void* stream, uint16_t* out, uint64_t seed, uint32_t slot_base,
     uint32_t slots, uint32_t layers, uint32_t heads_per_layer);
 
+/* Test support: quotients[i] = numerators[i] / divisors[i] computed with the
+ * quantizer's exact-division routine (RN(1/c) plus two fma corrections), for
+ * comparison with IEEE division.  Valid where that routine's preconditions
+ * hold (normal divisor and reciprocal, |numerator| >= 2^-102, normal
+ * quotient). */
+int32_t statecentric_gdn_state_codec_division_selftest_v1(
+    void* stream, const float* numerators, const float* divisors, float* quotients,
+    uint64_t count);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
