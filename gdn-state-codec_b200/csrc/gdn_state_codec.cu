@@ -97,7 +97,8 @@ int32_t run_quantize(void* stream, bool provider, int mode, const float* state,
   const DeviceSetup* s = device_setup();
   if (s == nullptr) return kSetupFailed;
   QuantizeParams p{state, smoothing_in, smoothing, codes, scales, items, map, status};
-  const int grid = grid_for(items, s->sms, s->quantize_blocks[provider][mode]);
+  const uint64_t units = (items + quantize_units_per_block() - 1) / quantize_units_per_block();
+  const int grid = grid_for(units, s->sms, s->quantize_blocks[provider][mode]);
   return launch_quantize(provider, mode, p, grid, static_cast<cudaStream_t>(stream)) ==
                  cudaSuccess
              ? kOk

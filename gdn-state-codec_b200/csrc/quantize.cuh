@@ -11,33 +11,33 @@
 //   z_kv = clamp(lround(s_kv / b_v * 127), -127, 127), 0 when b_v == 0
 //
 // Design (HBM-bound: 64 KiB read + 17 KiB written per head):
-//  * one persistent 512-thread CTA per SM with a ring of kStages 64 KiB
-//    shared-memory landing buffers, each filled by one TMA bulk copy
-//    (cp.async.bulk + mbarrier).  A buffer stays valid while its head is
-//    processed (the rare exact paths read it by run-time index) and is
-//    refilled once every thread has moved on, so kStages - 1 heads are always
-//    in flight behind the one being computed.
+//  * persistent 256-thread CTAs, two per SM.  Each walks its own sequence of
+//    heads with one 64 KiB shared-memory landing buffer filled by a single TMA
+//    bulk copy (cp.async.bulk + mbarrier); as soon as the CTA holds a head in
+//    registers the buffer takes its next head.  The two CTAs of an SM drift
+//    out of phase, so one's barriers and reductions overlap the other's
+//    arithmetic, and two heads are in flight per SM.
 //  * the smoothing sums run in double (tree order, with a proof-backed check
 //    that sends the rare order-sensitive rows to the reference's sequential
 //    order); every smoothed value s = R / c is computed correctly rounded from
 //    RN(1/c) by two packed fma corrections (div4_exact), so the per-value
 //    maxima b are exact without any search; codes come from one multiply by
-//    RN(127 / b) and the few elements within the proven error band of a
-//    rounding boundary are recomputed with IEEE division.
-//  * thread tiles keep the double-precision reduction mostly inside a thread:
-//    capsule layout (row sums over values) uses 4 rows x 8 columns per thread,
-//    provider layout (column sums over values) 8 rows x 4 columns; both read
-//    the landing buffer without bank conflicts.
+//    RN(127 / b), and the few elements within the proven error band of a
+//    rounding boundary take the exact code from the exact s.
+//  * thread tiles (64 elements per thread) keep the double-precision
+//    reduction mostly inside a thread: capsule layout (row sums over values)
+//    uses 4 rows x 16 columns, provider layout (column sums over values)
+//    16 rows x 4 columns; both read the landing buffer without bank conflicts.
 #pragma once
 
 #include "codec_device.cuh"
 
 namespace gdnsc {
 
-constexpr int kQThreads = 512;
-constexpr int kQWarps = kQThreads / 32;      // 16
-constexpr int kWarpRows = kKeys / kQWarps;   // 8 rows of a head per warp
-constexpr int kStages = 3;                   // TMA landing buffers per CTA
+constexpr int kQThreads = 256;
+constexpr int kQBlocksPerSm = 2;                    // independent head streams per SM
+constexpr int kGroupWarps = kQThreads / 32;         // 8
+constexpr int kWarpRows = kKeys / kGroupWarps;      // 16 rows of a head per warp
 
 // Codes: t' = RN(s * RN(127 / b)) and the exact t = RN(RN(s / b) * 127) both
 // lie within 2^-23 (relative, two roundings each) of s * 127 / b, so
@@ -49,7 +49,7 @@ constexpr float kAmbiguous = 0.5F - 0x1p-13F;
 // code (|s| >= b / 254) inside div4_exact's preconditions (|R| >= 2^-102,
 // normal quotient).  Smoothing computed here is always >= sqrt(1e-8) = 1e-4.
 // Values outside (all-zero or denormal columns, non-finite data, caller-given
-// smoothing out of range) take the IEEE path for the affected columns.
+// smoothing out of range) take the IEEE path for the affected values.
 constexpr float kFastMin = 0x1p-64F;
 constexpr float kFastMax = 0x1p100F;
 constexpr float kSmoothMin = 0x1p-14F;
@@ -71,42 +71,54 @@ struct QuantizeParams {
   uint32_t* status;           // optional caller status word
 };
 
-struct __align__(128) QuantizeShared {
-  float stage[kStages][kElements];  // TMA landing buffers (64 KiB each)
+// Shared state of one CTA.
+struct __align__(128) QuantizeGroupShared {
+  float stage[kElements];  // TMA landing buffer (64 KiB)
   union {
-    float col_part[kQWarps][kValues];  // capsule: per-warp column maxima
-    double col_dsum[kQWarps][kKeys];   // provider: per-warp column sums
+    float col_part[kGroupWarps][kValues];  // capsule: per-warp column maxima
+    double col_dsum[kGroupWarps][kKeys];   // provider: per-warp column sums
   };
-  float key_c[kKeys];               // provider: smoothing per key
-  float key_y[kKeys];               // provider: RN(1/c) per key
-  float col_b[kValues];             // capsule: exact per-value maximum
-  float col_km[kValues];            // capsule: RN(127 / b) (0 on the IEEE path)
-  uint32_t col_exact[kValues];      // capsule IEEE path: maximum (bits)
-  float colbuf[kKeys];              // provider: one column for a sequential re-sum
-  float row_c[kQWarps][kWarpRows];  // capsule: smoothing of the warp's rows
-  float row_y[kQWarps][kWarpRows];  // capsule: RN(1/c) of the warp's rows
-  float row_b[kQWarps][kWarpRows];  // provider: exact per-value maximum
-  float row_km[kQWarps][kWarpRows]; // provider: RN(127 / b) (0 on the IEEE path)
+  float key_c[kKeys];                  // smoothing per key
+  float key_y[kKeys];                  // RN(1/c) per key
+  float val_b[kValues];                // exact per-value maximum
+  float val_km[kValues];               // RN(127 / b), 0 on the IEEE path
+  uint32_t val_exact[kValues];         // IEEE path: maximum (bits)
+  float colbuf[kKeys];                 // provider: one column for a sequential re-sum
   int col_flag[kKeys];
-  uint64_t full[kStages];           // one mbarrier per landing buffer
+  uint64_t full;                       // mbarrier of the landing buffer
 };
+
+// Block-wide barriers (the CTA is one head stream).
+__device__ __forceinline__ void group_sync(int) { __syncthreads(); }
+__device__ __forceinline__ bool group_sync_or(int, bool pred) { return __syncthreads_or(pred) != 0; }
 
 // ---------------------------------------------------------------------------
 // Small helpers.
 
-__device__ __forceinline__ float4 absmax4v(float4 m, float4 a) {
-  return make_float4(fmaxf(m.x, fabsf(a.x)), fmaxf(m.y, fabsf(a.y)), fmaxf(m.z, fabsf(a.z)),
-                     fmaxf(m.w, fabsf(a.w)));
-}
-__device__ __forceinline__ float absmax4(float4 a) {
-  return fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
-}
 __device__ __forceinline__ float comp(const float4& a, int i) {
   return i == 0 ? a.x : (i == 1 ? a.y : (i == 2 ? a.z : a.w));
 }
 __device__ __forceinline__ double abs_sum4(float4 a) {
   return (static_cast<double>(fabsf(a.x)) + static_cast<double>(fabsf(a.y))) +
          (static_cast<double>(fabsf(a.z)) + static_cast<double>(fabsf(a.w)));
+}
+__device__ __forceinline__ float4 absmax4x4(float4 a, float4 b, float4 c, float4 d) {
+  return make_float4(fmaxf(fmaxf(fabsf(a.x), fabsf(b.x)), fmaxf(fabsf(c.x), fabsf(d.x))),
+                     fmaxf(fmaxf(fabsf(a.y), fabsf(b.y)), fmaxf(fabsf(c.y), fabsf(d.y))),
+                     fmaxf(fmaxf(fabsf(a.z), fabsf(b.z)), fmaxf(fabsf(c.z), fabsf(d.z))),
+                     fmaxf(fmaxf(fabsf(a.w), fabsf(b.w)), fmaxf(fabsf(c.w), fabsf(d.w))));
+}
+__device__ __forceinline__ float absmax4(float4 a) {
+  return fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+}
+__device__ __forceinline__ float4 fmax4(float4 a, float4 b) {
+  return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+}
+__device__ __forceinline__ float4 shfl_xor4(float4 v, int offset) {
+  return make_float4(__shfl_xor_sync(0xffffffffu, v.x, offset),
+                     __shfl_xor_sync(0xffffffffu, v.y, offset),
+                     __shfl_xor_sync(0xffffffffu, v.z, offset),
+                     __shfl_xor_sync(0xffffffffu, v.w, offset));
 }
 __device__ __forceinline__ bool fast_max(float b) { return b >= kFastMin && b <= kFastMax; }
 __device__ __forceinline__ bool fast_smoothing(float c) {
@@ -139,6 +151,17 @@ __device__ __forceinline__ bool approx_ambiguous(float s, float km) {
   return !(fabsf(d) <= kAmbiguous);
 }
 
+// Exact codes for the elements of one 4-element chunk that lie inside the
+// ambiguity band (s exact; b exact maximum; km = RN(127 / b)).
+__device__ __forceinline__ void patch_chunk(int8_t* dst, float4 s, float4 km, float4 b) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (comp(km, e) != 0.0F && approx_ambiguous(comp(s, e), comp(km, e))) {
+      dst[e] = exact_code(comp(s, e), comp(b, e));
+    }
+  }
+}
+
 // Next work item at or after `item` (stride `step`) that names a real head.
 __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t item,
                                               uint64_t step, int64_t* head, bool report_bad) {
@@ -156,87 +179,83 @@ __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t 
   return item;
 }
 
-__device__ __forceinline__ void issue_head(const QuantizeParams& p, float* buffer, uint64_t* bar,
+__device__ __forceinline__ void issue_head(const QuantizeParams& p, QuantizeGroupShared& gs,
                                            int64_t head) {
   fence_proxy_async();
-  mbar_expect_tx(bar, kElements * sizeof(float));
-  bulk_load(buffer, p.state + static_cast<uint64_t>(head) * kElements, kElements * sizeof(float),
-            bar, evict_first_policy());
+  mbar_expect_tx(&gs.full, kElements * sizeof(float));
+  bulk_load(gs.stage, p.state + static_cast<uint64_t>(head) * kElements, kElements * sizeof(float),
+            &gs.full, evict_first_policy());
+}
+
+__device__ __forceinline__ float state_at(const QuantizeParams& p, int64_t head, int row, int col) {
+  return __ldg(p.state + static_cast<uint64_t>(head) * kElements + row * 128 + col);
 }
 
 // ---------------------------------------------------------------------------
 // Capsule layout [key, value]: row k = key, column v = value.
 //
-// Thread tile: lane l = 16g + q (g = l/16, q = l%16) of warp w holds rows
-// r_j = 8w + 2j + g (j = 0..3) and, in each row, two 4-column chunks c = 0, 1
-// at columns 64c + 4q .. 64c + 4q + 3.  For a fixed (j, c) a half warp reads
-// 256 contiguous bytes of one row: conflict-free.  A row is shared by the 16
-// lanes of one g (row sums reduce over lane bits 0-3); a column by the two
-// lanes of one q (column maxima reduce over lane bit 4, then across warps).
+// Thread tile: lane l = 8g + q (g = l/8, q = l%8) of group warp w holds rows
+// r_j = 16w + 4j + g (j = 0..3) and, in each row, four 4-column chunks
+// c = 0..3 at columns 32c + 4q .. 32c + 4q + 3.  For a fixed (j, c) a quarter
+// warp reads 128 contiguous bytes of one row: conflict-free.  A row is shared
+// by the 8 lanes of one g (row sums reduce over lane bits 0-2); a column by
+// the 4 lanes of one q (column maxima reduce over lane bits 3-4, then across
+// the group's warps).
 
 struct CapsuleTile {
-  float4 v[4][2];  // [row j][chunk c]: R, then s = R / c
+  float4 v[4][4];  // [row j][chunk c]: R, then s = R / c
 };
 
-__device__ __forceinline__ void load_capsule_tile(const float* stage_f, CapsuleTile& t, int warp,
-                                                  int lane) {
-  const int g = lane >> 4, q = lane & 15;
-  const float4* stage = reinterpret_cast<const float4*>(stage_f);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int row = warp * kWarpRows + 2 * j + g;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) t.v[j][c] = stage[row * 32 + 16 * c + q];
-  }
-}
-
 template <int kMode>
-__device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p, QuantizeShared& sh,
-                                                      CapsuleTile& t, const float* stage,
-                                                      int64_t head, int warp, int lane, int tid) {
-  const int g = lane >> 4, q = lane & 15;
+__device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
+                                                      QuantizeGroupShared& gs, CapsuleTile& t,
+                                                      int64_t head, int group, int warp, int lane,
+                                                      int gtid) {
+  const int g = lane >> 3, q = lane & 7;
   const int row_base = warp * kWarpRows;
   // -- smoothing per row -----------------------------------------------------
-  bool bad_smoothing = false;
   if (kMode == kGivenSmoothing) {
     if (lane < kWarpRows) {
       const float c = __ldg(p.smoothing_in + head * kKeys + row_base + lane);
-      sh.row_c[warp][lane] = c;
-      sh.row_y[warp][lane] = __frcp_rn(c);
-      bad_smoothing = !fast_smoothing(c);
+      gs.key_c[row_base + lane] = c;
+      gs.key_y[row_base + lane] = __frcp_rn(c);
     }
   } else {
     double part[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) part[j] = abs_sum4(t.v[j][0]) + abs_sum4(t.v[j][1]);
-    // Reduce-scatter over the 16 lanes of this g (lane bits 3, 2), then sum
-    // over lane bits 1, 0: lanes 4i..4i+3 of the half warp hold row j = i.
-    {
-      const bool up = (lane & 8) != 0;
-      const double s0 = up ? part[0] : part[2], s1 = up ? part[1] : part[3];
-      const double k0 = up ? part[2] : part[0], k1 = up ? part[3] : part[1];
-      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 8);
-      part[1] = k1 + __shfl_xor_sync(0xffffffffu, s1, 8);
+    for (int j = 0; j < 4; ++j) {
+      part[j] = (abs_sum4(t.v[j][0]) + abs_sum4(t.v[j][1])) +
+                (abs_sum4(t.v[j][2]) + abs_sum4(t.v[j][3]));
     }
+    // Reduce-scatter over the 8 lanes of this g (lane bits 2, 1), then sum
+    // over lane bit 0: lanes 2i, 2i+1 of the group of 8 hold row j = i.
     {
       const bool up = (lane & 4) != 0;
+      const double s0 = up ? part[0] : part[2], s1 = up ? part[1] : part[3];
+      const double k0 = up ? part[2] : part[0], k1 = up ? part[3] : part[1];
+      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 4);
+      part[1] = k1 + __shfl_xor_sync(0xffffffffu, s1, 4);
+    }
+    {
+      const bool up = (lane & 2) != 0;
       const double s0 = up ? part[0] : part[1];
       const double k0 = up ? part[1] : part[0];
-      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 4);
+      part[0] = k0 + __shfl_xor_sync(0xffffffffu, s0, 2);
     }
-    double sum = part[0] + __shfl_xor_sync(0xffffffffu, part[0], 2);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    const int my_j = (lane >> 2) & 3;  // this lane group's row r = 8w + 2*my_j + g
+    double sum = part[0] + __shfl_xor_sync(0xffffffffu, part[0], 1);
+    const int my_j = (lane >> 1) & 3;  // this lane pair's row r = 16w + 4*my_j + g
     // Rows whose float mean could depend on the summation order are re-summed
-    // in the reference's order (capsule.cpp:193-196): value 0..127, read from
-    // the landing buffer.  Rare.
+    // in the reference's order (capsule.cpp:193-196): value 0..127, re-read
+    // from the input.  Rare.
     uint32_t flagged =
-        __ballot_sync(0xffffffffu, near_float_midpoint(sum * (1.0 / 128.0))) & 0x11111111u;
+        __ballot_sync(0xffffffffu, near_float_midpoint(sum * (1.0 / 128.0))) & 0x55555555u;
     while (flagged != 0u) {
       const int owner = __ffs(flagged) - 1;
       flagged &= flagged - 1u;
-      const int row = row_base + 2 * ((owner >> 2) & 3) + (owner >> 4);
-      const float4 mine = reinterpret_cast<const float4*>(stage)[row * 32 + lane];
+      const int row = row_base + 4 * ((owner >> 1) & 3) + (owner >> 3);
+      const float4 mine = __ldg(reinterpret_cast<const float4*>(
+                                    p.state + static_cast<uint64_t>(head) * kElements + row * 128) +
+                                lane);
       double seq = 0.0;
       for (int src = 0; src < 32; ++src) {
         seq += fabsf(__shfl_sync(0xffffffffu, mine.x, src));
@@ -244,120 +263,124 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p, Q
         seq += fabsf(__shfl_sync(0xffffffffu, mine.z, src));
         seq += fabsf(__shfl_sync(0xffffffffu, mine.w, src));
       }
-      if ((lane >> 2) == (owner >> 2)) sum = seq;
+      if ((lane >> 1) == (owner >> 1)) sum = seq;
     }
     const float c = smoothing_from_sum(sum);
-    if ((lane & 3) == 0) {
-      const int r = 2 * my_j + g;
-      sh.row_c[warp][r] = c;
-      sh.row_y[warp][r] = __frcp_rn(c);
-      p.smoothing[head * kKeys + row_base + r] = c;
+    if ((lane & 1) == 0) {
+      const int r = row_base + 4 * my_j + g;
+      gs.key_c[r] = c;
+      gs.key_y[r] = __frcp_rn(c);
+      p.smoothing[head * kKeys + r] = c;
     }
   }
   __syncwarp();
   if (kMode == kSmoothingOnly) return;
 
   // -- exact smoothed values and column maxima ------------------------------------
-  float4 pm[2] = {make_float4(0.F, 0.F, 0.F, 0.F), make_float4(0.F, 0.F, 0.F, 0.F)};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float y = sh.row_y[warp][2 * j + g];
-    const float nc = -sh.row_c[warp][2 * j + g];
+    const int r = row_base + 4 * j + g;
+    const float y = gs.key_y[r];
+    const float nc = -gs.key_c[r];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      t.v[j][c] = div4_exact_s(t.v[j][c], y, nc);
-      pm[c] = absmax4v(pm[c], t.v[j][c]);
+    for (int c = 0; c < 4; ++c) t.v[j][c] = div4_exact_s(t.v[j][c], y, nc);
+  }
+  float4 pm[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) pm[c] = absmax4x4(t.v[0][c], t.v[1][c], t.v[2][c], t.v[3][c]);
+  // Reduce-scatter over lane bits 4, 3: afterwards this lane holds the warp
+  // maximum of chunk c = g (columns 32g + 4q ..).
+  float4 red[2];
+  {
+    const bool up = (lane & 16) != 0;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float4 send = up ? pm[i] : pm[i + 2];
+      const float4 keep = up ? pm[i + 2] : pm[i];
+      red[i] = fmax4(keep, shfl_xor4(send, 16));
     }
   }
   {
-    // Exchange over lane bit 4: afterwards this lane holds the warp maximum
-    // of chunk c = g (columns 64g + 4q ..).
-    const bool up = (lane & 16) != 0;
-    const float4 send = up ? pm[0] : pm[1];
-    const float4 keep = up ? pm[1] : pm[0];
-    const float4 m = make_float4(fmaxf(keep.x, __shfl_xor_sync(0xffffffffu, send.x, 16)),
-                                 fmaxf(keep.y, __shfl_xor_sync(0xffffffffu, send.y, 16)),
-                                 fmaxf(keep.z, __shfl_xor_sync(0xffffffffu, send.z, 16)),
-                                 fmaxf(keep.w, __shfl_xor_sync(0xffffffffu, send.w, 16)));
-    reinterpret_cast<float4*>(sh.col_part[warp])[16 * g + q] = m;
+    const bool up = (lane & 8) != 0;
+    const float4 send = up ? red[0] : red[1];
+    const float4 keep = up ? red[1] : red[0];
+    reinterpret_cast<float4*>(gs.col_part[warp])[8 * g + q] = fmax4(keep, shfl_xor4(send, 8));
   }
-  const bool head_slow = __syncthreads_or(bad_smoothing) != 0;  // B1
-  int slow = 0;
-  if (tid < kValues) {
+  group_sync(group);  // B1: column partial maxima and smoothing published
+  bool slow = false;
+  if (gtid < kValues) {
+    // Caller-given smoothing out of the fast range sends the whole head to
+    // the IEEE path; each of these warps checks all 128 keys itself, so no
+    // barrier result has to stay live into this branch.
+    bool head_slow = false;
+    if (kMode == kGivenSmoothing) {
+      const float4 c4 = reinterpret_cast<const float4*>(gs.key_c)[lane];
+      head_slow = __any_sync(0xffffffffu, !(fast_smoothing(c4.x) && fast_smoothing(c4.y) &&
+                                            fast_smoothing(c4.z) && fast_smoothing(c4.w)));
+    }
     float b = 0.0F;
 #pragma unroll
-    for (int w = 0; w < kQWarps; ++w) b = fmaxf(b, sh.col_part[w][tid]);
+    for (int w = 0; w < kGroupWarps; ++w) b = fmaxf(b, gs.col_part[w][gtid]);
     slow = head_slow || !fast_max(b);
-    sh.col_b[tid] = b;
-    sh.col_km[tid] = slow ? 0.0F : __fdiv_rn(kQuantMax, b);
-    sh.col_exact[tid] = 0u;
-    if (!slow) p.scales[head * kValues + tid] = b;
+    gs.val_b[gtid] = b;
+    gs.val_km[gtid] = slow ? 0.0F : __fdiv_rn(kQuantMax, b);
+    gs.val_exact[gtid] = 0u;
+    if (!slow) p.scales[head * kValues + gtid] = b;
   }
-  const bool any_slow = __syncthreads_or(slow) != 0;  // B2
+  const bool any_slow = group_sync_or(group, slow);  // B2
 
   // -- codes ----------------------------------------------------------------------
-  uint32_t amb_mask = 0u;  // bit 2j+c: chunk (j, c) holds an ambiguous element
   int8_t* codes = p.codes + static_cast<uint64_t>(head) * kElements;
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const float4 km = reinterpret_cast<const float4*>(sh.col_km)[16 * c + q];
+  for (int c = 0; c < 4; ++c) {
+    const float4 km = reinterpret_cast<const float4*>(gs.val_km)[8 * c + q];
+    uint32_t amb_rows = 0u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       bool amb;
       const uint32_t word = approx_codes(t.v[j][c], km, &amb);
-      st_cs_u32(codes + (row_base + 2 * j + g) * kValues + 64 * c + 4 * q, word);
-      amb_mask |= (amb ? 1u : 0u) << (2 * j + c);
+      st_cs_u32(codes + (row_base + 4 * j + g) * kValues + 32 * c + 4 * q, word);
+      amb_rows |= (amb ? 1u : 0u) << j;
     }
-  }
-  // Elements inside the ambiguity band take the exact code (IEEE division
-  // from the landing buffer, exact maximum).
-  while (amb_mask != 0u) {
-    const int bit = __ffs(amb_mask) - 1;
-    amb_mask &= amb_mask - 1u;
-    const int r_local = 2 * (bit >> 1) + g, c = bit & 1;
-    const float c_r = sh.row_c[warp][r_local];
-    const float y_r = sh.row_y[warp][r_local];
-    for (int e = 0; e < 4; ++e) {
-      const int col = 64 * c + 4 * q + e;
-      const float km = sh.col_km[col];
-      if (km == 0.0F) continue;  // IEEE-path column, handled below
-      const float r = stage[(row_base + r_local) * kValues + col];
-      if (approx_ambiguous(div4_exact_s(make_float4(r, 0.F, 0.F, 0.F), y_r, -c_r).x, km)) {
-        codes[(row_base + r_local) * kValues + col] = exact_code(__fdiv_rn(r, c_r), sh.col_b[col]);
+    if (amb_rows != 0u) {  // rare: exact codes from the exact s
+      const float4 b = reinterpret_cast<const float4*>(gs.val_b)[8 * c + q];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if ((amb_rows >> j) & 1u) {
+          patch_chunk(codes + (row_base + 4 * j + g) * kValues + 32 * c + 4 * q, t.v[j][c], km, b);
+        }
       }
     }
   }
   if (any_slow) {
-    // IEEE path for columns outside the fast ranges (rare; all-zero columns
-    // included): exact quotients, an exact maximum across the block, codes.
+    // IEEE path for values outside the fast ranges: exact quotients from the
+    // input, exact maxima across the group, then codes.  Rare.
     for (int j = 0; j < 4; ++j) {
-      const int r_local = 2 * j + g;
-      for (int c = 0; c < 2; ++c) {
+      const int r = row_base + 4 * j + g;
+      for (int c = 0; c < 4; ++c) {
         for (int e = 0; e < 4; ++e) {
-          const int col = 64 * c + 4 * q + e;
-          if (sh.col_km[col] != 0.0F) continue;
-          const float r = stage[(row_base + r_local) * kValues + col];
-          if (r != 0.0F) {
-            atomicMax(&sh.col_exact[col],
-                      __float_as_uint(fabsf(__fdiv_rn(r, sh.row_c[warp][r_local]))));
+          const int col = 32 * c + 4 * q + e;
+          if (gs.val_km[col] != 0.0F) continue;
+          const float x = state_at(p, head, r, col);
+          if (x != 0.0F) {
+            atomicMax(&gs.val_exact[col], __float_as_uint(fabsf(__fdiv_rn(x, gs.key_c[r]))));
           }
         }
       }
     }
-    __syncthreads();
-    if (tid < kValues && sh.col_km[tid] == 0.0F) {
-      p.scales[head * kValues + tid] = __uint_as_float(sh.col_exact[tid]);
+    group_sync(group);
+    if (gtid < kValues && gs.val_km[gtid] == 0.0F) {
+      p.scales[head * kValues + gtid] = __uint_as_float(gs.val_exact[gtid]);
     }
     for (int j = 0; j < 4; ++j) {
-      const int r_local = 2 * j + g;
-      for (int c = 0; c < 2; ++c) {
+      const int r = row_base + 4 * j + g;
+      for (int c = 0; c < 4; ++c) {
         for (int e = 0; e < 4; ++e) {
-          const int col = 64 * c + 4 * q + e;
-          if (sh.col_km[col] != 0.0F) continue;
-          const float r = stage[(row_base + r_local) * kValues + col];
-          codes[(row_base + r_local) * kValues + col] =
-              exact_code(r == 0.0F ? 0.0F : __fdiv_rn(r, sh.row_c[warp][r_local]),
-                         __uint_as_float(sh.col_exact[col]));
+          const int col = 32 * c + 4 * q + e;
+          if (gs.val_km[col] != 0.0F) continue;
+          const float x = state_at(p, head, r, col);
+          codes[r * kValues + col] = exact_code(x == 0.0F ? 0.0F : __fdiv_rn(x, gs.key_c[r]),
+                                                __uint_as_float(gs.val_exact[col]));
         }
       }
     }
@@ -366,16 +389,16 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p, Q
 
 // ---------------------------------------------------------------------------
 // Provider layout [value, key]: row = value v, column = key k.
-// Thread tile: warp w holds rows 8w..8w+7, lane l columns 4l..4l+3 (a warp
-// reads one 512-byte row per instruction: conflict-free).
+// Thread tile: group warp w holds rows 16w..16w+15, lane l columns 4l..4l+3
+// (a warp reads one 512-byte row per instruction: conflict-free).
 
 template <int kMode>
-__device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, QuantizeShared& sh,
-                                                       float4 (&v)[kWarpRows], const float* stage,
-                                                       int64_t head, int warp, int lane,
-                                                       int tid) {
+__device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
+                                                       QuantizeGroupShared& gs,
+                                                       float4 (&v)[kWarpRows], int64_t head,
+                                                       int group, int warp, int lane, int gtid) {
   const int row_base = warp * kWarpRows;
-  // -- smoothing per key (column): thread-local over 8 rows, then across warps
+  // -- smoothing per key (column): thread-local over 16 rows, then across warps
   if (kMode != kGivenSmoothing) {
     double cs0 = 0.0, cs1 = 0.0, cs2 = 0.0, cs3 = 0.0;
 #pragma unroll
@@ -385,57 +408,59 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, 
       cs2 += fabsf(v[j].z);
       cs3 += fabsf(v[j].w);
     }
-    double* dst = &sh.col_dsum[warp][4 * lane];
+    double* dst = &gs.col_dsum[warp][4 * lane];
     dst[0] = cs0;
     dst[1] = cs1;
     dst[2] = cs2;
     dst[3] = cs3;
   }
-  __syncthreads();  // B1: column partial sums published
+  group_sync(group);  // B1: column partial sums published
   int flag = 0;
   bool bad_smoothing = false;
-  if (tid < kKeys) {
+  if (gtid < kKeys) {
     float c;
     if (kMode == kGivenSmoothing) {
-      c = __ldg(p.smoothing_in + head * kKeys + tid);
+      c = __ldg(p.smoothing_in + head * kKeys + gtid);
       bad_smoothing = !fast_smoothing(c);
     } else {
       double sum = 0.0;
 #pragma unroll
-      for (int w = 0; w < kQWarps; ++w) sum += sh.col_dsum[w][tid];
+      for (int w = 0; w < kGroupWarps; ++w) sum += gs.col_dsum[w][gtid];
       flag = near_float_midpoint(sum * (1.0 / 128.0));
       c = smoothing_from_sum(sum);
-      if (!flag) p.smoothing[head * kKeys + tid] = c;
+      if (!flag) p.smoothing[head * kKeys + gtid] = c;
     }
-    sh.key_c[tid] = c;
-    sh.key_y[tid] = __frcp_rn(c);
-    sh.col_flag[tid] = flag;
+    gs.key_c[gtid] = c;
+    gs.key_y[gtid] = __frcp_rn(c);
+    gs.col_flag[gtid] = flag;
   }
-  // B2: smoothing ready; bit 0 = a column needs the sequential re-sum,
-  // bit 1 = caller-given smoothing outside the fast range.
-  const int b2 = __syncthreads_or(flag | (bad_smoothing ? 2 : 0));
-  if (b2 & 1) {  // rare, block-uniform
+  // B2: smoothing ready.  With computed smoothing it also tells whether a
+  // column needs the sequential re-sum; with caller-given smoothing, whether a
+  // value left the fast range.
+  const bool b2 = group_sync_or(group, kMode == kGivenSmoothing ? bad_smoothing : flag != 0);
+  const bool any_flag = kMode != kGivenSmoothing && b2;
+  const bool head_slow = kMode == kGivenSmoothing && b2;
+  if (any_flag) {  // rare, group-uniform
     for (int k = 0; k < kKeys; ++k) {
-      if (!sh.col_flag[k]) continue;
-      if (tid < kValues) sh.colbuf[tid] = stage[tid * kKeys + k];
-      __syncthreads();
-      if (tid == 0) {
+      if (!gs.col_flag[k]) continue;
+      if (gtid < kValues) gs.colbuf[gtid] = state_at(p, head, gtid, k);
+      group_sync(group);
+      if (gtid == 0) {
         double seq = 0.0;  // capsule.cpp:193-196 order: value 0..127
-        for (int r = 0; r < kValues; ++r) seq += fabsf(sh.colbuf[r]);
+        for (int r = 0; r < kValues; ++r) seq += fabsf(gs.colbuf[r]);
         const float c = smoothing_from_sum(seq);
-        sh.key_c[k] = c;
-        sh.key_y[k] = __frcp_rn(c);
+        gs.key_c[k] = c;
+        gs.key_y[k] = __frcp_rn(c);
         p.smoothing[head * kKeys + k] = c;
       }
-      __syncthreads();
+      group_sync(group);
     }
   }
   if (kMode == kSmoothingOnly) return;
-  const bool head_slow = (b2 & 2) != 0;
 
   // -- exact smoothed values and row maxima (warp-local) ------------------------------
-  const float4 c4 = reinterpret_cast<const float4*>(sh.key_c)[lane];
-  const float4 y4 = reinterpret_cast<const float4*>(sh.key_y)[lane];
+  const float4 c4 = reinterpret_cast<const float4*>(gs.key_c)[lane];
+  const float4 y4 = reinterpret_cast<const float4*>(gs.key_y)[lane];
   const float4 nc4 = make_float4(-c4.x, -c4.y, -c4.z, -c4.w);
   float rm[kWarpRows];
 #pragma unroll
@@ -456,40 +481,37 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, 
       }
     }
   }
-  float b = fmaxf(rm[0], __shfl_xor_sync(0xffffffffu, rm[0], 2));
-  b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, 1));
-  const int my_row = lane >> 2;  // lanes 4r..4r+3 hold row r
+  const float b = fmaxf(rm[0], __shfl_xor_sync(0xffffffffu, rm[0], 1));
+  const int my_row = lane >> 1;  // lanes 2r, 2r+1 hold row r
   const bool my_slow = head_slow || !fast_max(b);
-  if ((lane & 3) == 0) {
-    sh.row_b[warp][my_row] = b;
-    sh.row_km[warp][my_row] = my_slow ? 0.0F : __fdiv_rn(kQuantMax, b);
-    if (!my_slow) p.scales[head * kValues + row_base + my_row] = b;
+  const int vrow = row_base + my_row;
+  if ((lane & 1) == 0) {
+    gs.val_b[vrow] = b;
+    gs.val_km[vrow] = my_slow ? 0.0F : __fdiv_rn(kQuantMax, b);
+    if (!my_slow) p.scales[head * kValues + vrow] = b;
   }
-  const uint32_t slow_rows = __ballot_sync(0xffffffffu, my_slow && (lane & 3) == 0);
+  const uint32_t slow_rows = __ballot_sync(0xffffffffu, my_slow && (lane & 1) == 0);
   __syncwarp();
 
   // -- codes ------------------------------------------------------------------------
-  uint32_t amb_rows = 0u;
   int8_t* codes = p.codes + static_cast<uint64_t>(head) * kElements;
+  uint32_t amb_rows = 0u;
 #pragma unroll
   for (int j = 0; j < kWarpRows; ++j) {
-    const float km = sh.row_km[warp][j];
+    const float km = gs.val_km[row_base + j];
     bool amb;
     const uint32_t word = approx_codes(v[j], make_float4(km, km, km, km), &amb);
     st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
     amb_rows |= (amb ? 1u : 0u) << j;
   }
-  while (amb_rows != 0u) {
-    const int j = __ffs(amb_rows) - 1;
-    amb_rows &= amb_rows - 1u;
-    const float km = sh.row_km[warp][j];
-    if (km == 0.0F) continue;  // IEEE-path row, handled below
-    const float4 r4 = reinterpret_cast<const float4*>(stage)[(row_base + j) * 32 + lane];
-    const float4 s4 = div4_exact(r4, y4, nc4);
-    for (int i = 0; i < 4; ++i) {
-      if (approx_ambiguous(comp(s4, i), km)) {
-        codes[(row_base + j) * kKeys + 4 * lane + i] =
-            exact_code(__fdiv_rn(comp(r4, i), comp(c4, i)), sh.row_b[warp][j]);
+  if (amb_rows != 0u) {  // rare: exact codes from the exact s
+#pragma unroll
+    for (int j = 0; j < kWarpRows; ++j) {
+      if ((amb_rows >> j) & 1u) {
+        const float km = gs.val_km[row_base + j];
+        const float bb = gs.val_b[row_base + j];
+        patch_chunk(codes + (row_base + j) * kKeys + 4 * lane, v[j], make_float4(km, km, km, km),
+                    make_float4(bb, bb, bb, bb));
       }
     }
   }
@@ -498,8 +520,11 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, 
   while (slow_left != 0u) {
     const int owner = __ffs(slow_left) - 1;
     slow_left &= slow_left - 1u;
-    const int j = owner >> 2;
-    const float4 r4 = reinterpret_cast<const float4*>(stage)[(row_base + j) * 32 + lane];
+    const int j = owner >> 1;
+    const float4 r4 = __ldg(reinterpret_cast<const float4*>(
+                                p.state + static_cast<uint64_t>(head) * kElements +
+                                (row_base + j) * 128) +
+                            lane);
     float4 s4;
     s4.x = r4.x == 0.0F ? 0.0F : __fdiv_rn(r4.x, c4.x);
     s4.y = r4.y == 0.0F ? 0.0F : __fdiv_rn(r4.y, c4.y);
@@ -520,77 +545,67 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p, 
 // ---------------------------------------------------------------------------
 
 template <bool kProvider, int kMode>
-__global__ void __launch_bounds__(kQThreads, 1) quantize_kernel(QuantizeParams p) {
+__global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(QuantizeParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  QuantizeShared& sh = *reinterpret_cast<QuantizeShared*>(smem_raw);
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
+  QuantizeGroupShared& gs = *reinterpret_cast<QuantizeGroupShared*>(smem_raw);
+  const int group = 0;
+  const int gtid = threadIdx.x;
+  const int warp = gtid >> 5;
+  const int lane = gtid & 31;
+  // Block b takes items b, b + G, b + 2G, ... (G = gridDim.x).
   const uint64_t step = gridDim.x;
+  const uint64_t first = blockIdx.x;
 
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&sh.full[s], 1);
+  if (gtid == 0) {
+    mbar_init(&gs.full, 1);
     fence_mbar_init();
   }
   __syncthreads();
 
-  // The producer (thread 0) runs kStages valid heads ahead of the consumers;
-  // both walk the same deterministic item sequence.  Head number n lives in
-  // landing buffer n % kStages, whose fill for it has parity (n / kStages) & 1.
-  int64_t prod_head = -1;
-  uint64_t prod_item = 0;
-  uint32_t issued = 0;
-  if (tid == 0) {
-    prod_item = next_item(p, blockIdx.x, step, &prod_head, false);
-    for (int s = 0; s < kStages && prod_head >= 0; ++s) {
-      issue_head(p, sh.stage[s], &sh.full[s], prod_head);
-      ++issued;
-      prod_item = next_item(p, prod_item + step, step, &prod_head, false);
-    }
-  }
   int64_t head = -1;
-  uint64_t item = next_item(p, blockIdx.x, step, &head, tid == 0);
-  uint32_t consumed = 0;
+  uint64_t item = next_item(p, first, step, &head, gtid == 0);
+  if (gtid == 0 && head >= 0) issue_head(p, gs, head);
+  uint32_t parity = 0;
   while (head >= 0) {
-    const int stage = static_cast<int>(consumed % kStages);
-    const bool timed_out = !mbar_wait_bounded(&sh.full[stage], (consumed / kStages) & 1u);
+    const bool timed_out = !mbar_wait_bounded(&gs.full, parity);
+    parity ^= 1u;
     CapsuleTile ct;
     float4 pv[kWarpRows];
     if (kProvider) {
-      const float4* src = reinterpret_cast<const float4*>(sh.stage[stage]);
+      const float4* src = reinterpret_cast<const float4*>(gs.stage);
 #pragma unroll
       for (int j = 0; j < kWarpRows; ++j) pv[j] = src[(warp * kWarpRows + j) * 32 + lane];
     } else {
-      load_capsule_tile(sh.stage[stage], ct, warp, lane);
+      const int g = lane >> 3, q = lane & 7;
+      const float4* src = reinterpret_cast<const float4*>(gs.stage);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int row = warp * kWarpRows + 4 * j + g;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) ct.v[j][c] = src[row * 32 + 8 * c + q];
+      }
     }
-    ++consumed;
-    // B0: every warp holds its part of this head and has finished the previous
-    // one, whose landing buffer now takes the head kStages - 1 ahead.
-    if (__syncthreads_or(timed_out) != 0) {
-      // A bounded wait expired: report it, then wait, again bounded, for every
-      // copy that may still be in flight (fills consumed-1 .. issued-1) so that
-      // none lands in this block's shared memory after it exits.  Outputs of
-      // this launch are then unspecified.
-      if (tid == 0) {
+    int64_t next_head = -1;
+    const uint64_t next = next_item(p, item + step, step, &next_head, gtid == 0);
+    // B0: the group holds this head in registers; the buffer takes the next.
+    if (group_sync_or(group, timed_out)) {
+      // A bounded wait expired: report it and let the copy in flight land
+      // (again bounded) so no bulk copy targets this block after it exits.
+      // Outputs of this launch are then unspecified.
+      if (gtid == 0) {
         report(p.status, kStatusWaitTimeout);
-        for (uint32_t n = consumed - 1u; n < issued; ++n) {
-          (void)mbar_wait_bounded(&sh.full[n % kStages], (n / kStages) & 1u);
-        }
+        if (timed_out) (void)mbar_wait_bounded(&gs.full, parity ^ 1u);
       }
       return;
     }
-    if (tid == 0 && consumed >= 2 && prod_head >= 0) {
-      const int prev = static_cast<int>((consumed - 2) % kStages);
-      issue_head(p, sh.stage[prev], &sh.full[prev], prod_head);
-      ++issued;
-      prod_item = next_item(p, prod_item + step, step, &prod_head, false);
-    }
+    if (gtid == 0 && next_head >= 0) issue_head(p, gs, next_head);
     if (kProvider) {
-      quantize_provider_head<kMode>(p, sh, pv, sh.stage[stage], head, warp, lane, tid);
+      quantize_provider_head<kMode>(p, gs, pv, head, group, warp, lane, gtid);
     } else {
-      quantize_capsule_head<kMode>(p, sh, ct, sh.stage[stage], head, warp, lane, tid);
+      quantize_capsule_head<kMode>(p, gs, ct, head, group, warp, lane, gtid);
     }
-    item = next_item(p, item + step, step, &head, tid == 0);
+    item = next;
+    head = next_head;
   }
 }
 
@@ -602,7 +617,7 @@ cudaError_t launch_quantize_t(const QuantizeParams& p, int grid, cudaStream_t st
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kQThreads);
-  cfg.dynamicSmemBytes = sizeof(QuantizeShared);
+  cfg.dynamicSmemBytes = sizeof(QuantizeGroupShared);
   cfg.stream = stream;
   return cudaLaunchKernelEx(&cfg, quantize_kernel<kProvider, kMode>, p);
 }
@@ -611,11 +626,14 @@ template <bool kProvider, int kMode>
 cudaError_t prepare_quantize_t(int* blocks_per_sm) {
   auto kernel = quantize_kernel<kProvider, kMode>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(sizeof(QuantizeShared)));
+                                         static_cast<int>(sizeof(QuantizeGroupShared)));
   if (err != cudaSuccess) return err;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, kernel, kQThreads,
-                                                       sizeof(QuantizeShared));
+                                                       sizeof(QuantizeGroupShared));
 }
+
+// Work units of a launch are heads; one head is processed per block at a time.
+inline int quantize_units_per_block() { return 1; }
 
 inline cudaError_t prepare_quantize(bool provider, int mode, int* blocks_per_sm) {
   if (provider) {
