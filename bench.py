@@ -2,9 +2,9 @@
 
 One step = one pass of the codec over one batch: int8 quantize (fused
 smoothing) of every head of the workload, then dequantize of every head
-(30 GDN layers x 64 request slots x fp32 state
-[32, 128, 128] = 61,440 heads, ~4 GB fp32 + 1.07 GB codes, contiguous
-slot-major cache, capsule layout).  Under torchrun each rank owns its own 64
+(the batched full-model configuration: 30 GDN layers x 64 request slots x
+fp32 state [32, 128, 128] = 61,440 heads, ~4 GB fp32 + 1.07 GB codes,
+contiguous slot-major cache, capsule layout).  Under torchrun each rank owns its own 64
 slots (weak scaling, no data-path collective); rank r's slots are global slots
 64r..64r+63 of the seeded synthetic generator.
 
@@ -224,7 +224,7 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    from gdn_state_codec import codec
+    from gdn_state_codec import codec, sharding
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -240,22 +240,18 @@ def main() -> None:
                                 device_id=device)
 
     def barrier():
-        if world > 1:
-            dist.barrier()
+        sharding.barrier()
         torch.cuda.synchronize(device)
 
     def max_over_ranks(value: float) -> float:
-        if world == 1:
-            return value
-        t = torch.tensor([value], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(value, device=device)
 
-    slots = args.slots
+    shard = sharding.weak_shard(rank, world, args.slots)
+    slots = shard.count
     heads = slots * LAYERS * HEADS
     layout = args.layout
     states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=0,
-                                     slot_base=rank * slots, device=device)
+                                     slot_base=shard.base, device=device)
     encoded = codec.empty_encoded((slots, LAYERS, HEADS), layout, device)
     dense = torch.empty_like(states)
     stream = torch.cuda.current_stream(device)
@@ -308,7 +304,7 @@ def main() -> None:
     value = world * heads * args.steps / (elapsed_ms / 1e3)
 
     # ---- encoded projection over the same 30-layer cache (config 3 kernel) ----
-    queries = codec.synthesize_queries(slots, LAYERS, HEADS, seed=1, slot_base=rank * slots,
+    queries = codec.synthesize_queries(slots, LAYERS, HEADS, seed=1, slot_base=shard.base,
                                        device=device)
     outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
     for _ in range(3):

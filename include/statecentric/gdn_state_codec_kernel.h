@@ -135,8 +135,8 @@ int32_t statecentric_gdn_state_codec_provider_encoded_projection_launch_v1(
  * `heads_per_slot` heads each (slot-major: head index slot*heads_per_slot+h).
  * `slot_ids` is a device array of `count` int32 ids (any order, may repeat
  * only for read-only use); id -1 (PAD_SLOT_ID) is skipped; ids outside
- * [-1, num_slots) are skipped and set bit 1 in *status (device uint32,
- * optional) and in the library's sticky error word.  `layout` is 0 for
+ * [-1, num_slots) are skipped and set bit 0 (value 1) in *status (device
+ * uint32, optional) and in the library's sticky error word.  `layout` is 0 for
  * capsule, 1 for provider.  The vLLM runtime range-checks its cache index on
  * the host (runtime.py:607-608); these kernels check on the device instead. */
 

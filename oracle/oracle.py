@@ -263,3 +263,80 @@ def ref_codec_head(dense: np.ndarray, query: np.ndarray | None = None) -> dict:
     if q is None:
         del out["projection"]
     return out
+
+
+# --------------------------------------------------------------------------
+# The reference's own quant-only stage (ref_quant_shim.cpp: QuantizeBoundary,
+# DequantizeBoundary and ReadWindowState of capsule.cpp at compensator rank 0).
+# Capsule layout only: the reference has no provider-layout CPU path.
+
+REF_QUANT_LIB_PATH = ORACLE_DIR / "_ref" / "libgdn_ref_quant.so"
+_ref_quant = None
+
+
+def ref_quant_available() -> bool:
+    return REF_QUANT_LIB_PATH.is_file()
+
+
+def ref_quant() -> ctypes.CDLL:
+    global _ref_quant
+    if _ref_quant is None:
+        if not REF_QUANT_LIB_PATH.is_file():
+            raise RuntimeError(f"reference quant-only library not built: {REF_QUANT_LIB_PATH}")
+        handle = ctypes.CDLL(str(REF_QUANT_LIB_PATH))
+        u64, u32, c_int = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int
+        handle.ref_quant_only_encode.argtypes = [
+            _f32p, u64, u32, u32, c_int, _i8p, _f32p, _f32p]
+        handle.ref_quant_only_decode.argtypes = [
+            _i8p, _f32p, _f32p, u64, u32, u32, c_int, _f32p]
+        handle.ref_quant_only_project.argtypes = [
+            _i8p, _f32p, _f32p, _f32p, u64, u32, u32, c_int, _f32p]
+        for name in ("ref_quant_only_encode", "ref_quant_only_decode",
+                     "ref_quant_only_project"):
+            getattr(handle, name).restype = c_int
+        _ref_quant = handle
+    return _ref_quant
+
+
+def ref_quant_encode(state: np.ndarray, threads: int = 1):
+    """Reference quant-only encode of capsule heads: (codes, smoothing, scales)."""
+    state = np.ascontiguousarray(state, dtype=np.float32)
+    heads, keys, values = state.shape
+    codes = np.empty(state.shape, np.int8)
+    c = np.empty((heads, keys), np.float32)
+    b = np.empty((heads, values), np.float32)
+    status = ref_quant().ref_quant_only_encode(
+        _ptr(state, _f32p), heads, keys, values, threads, _ptr(codes, _i8p), _ptr(c, _f32p),
+        _ptr(b, _f32p))
+    if status != 0:
+        raise ValueError("reference quantizer rejected the input")
+    return codes, c, b
+
+
+def ref_quant_decode(codes, c, b, threads: int = 1) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    c = np.ascontiguousarray(c, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    heads, keys, values = codes.shape
+    dense = np.empty(codes.shape, np.float32)
+    status = ref_quant().ref_quant_only_decode(
+        _ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p), heads, keys, values, threads,
+        _ptr(dense, _f32p))
+    if status != 0:
+        raise ValueError("reference dequantizer rejected the input")
+    return dense
+
+
+def ref_quant_project(codes, c, b, queries, threads: int = 1) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    c = np.ascontiguousarray(c, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    q = np.ascontiguousarray(queries, dtype=np.float32)
+    heads, keys, values = codes.shape
+    out = np.empty((heads, values), np.float32)
+    status = ref_quant().ref_quant_only_project(
+        _ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p), _ptr(q, _f32p), heads, keys, values,
+        threads, _ptr(out, _f32p))
+    if status != 0:
+        raise ValueError("reference readout rejected the input")
+    return out

@@ -27,4 +27,5 @@ def golden():
         "heads": dict(np.load(GOLDEN / "reference_heads.npz")),
         "small": dict(np.load(GOLDEN / "reference_small.npz")),
         "adapter": dict(np.load(GOLDEN / "adapter.npz")),
+        "quant_only": dict(np.load(GOLDEN / "reference_quant_only.npz")),
     }

@@ -23,6 +23,12 @@ Files:
                        (gdn_state_codec_state_capsule_test.cpp:40-48).
   adapter.npz          provider->capsule transpose of the reference adapter
                        test (gdn_state_codec_qwen38_gdn_adapter_test.cpp:20-31).
+  reference_quant_only.npz
+                       the reference's own quant-only stage (QuantizeBoundary,
+                       DequantizeBoundary, ReadWindowState of capsule.cpp at
+                       compensator rank 0, via oracle/ref_quant_shim.cpp) on
+                       benchmark heads and edge cases: input, codes, smoothing,
+                       scales, dense reconstruction, query and readout.
 """
 
 from __future__ import annotations
@@ -109,7 +115,42 @@ def main() -> None:
     assert status == 0
     np.savez_compressed(OUT / "adapter.npz", provider=provider.reshape(2, 3),
                         capsule=capsule.reshape(3, 2))
+    quant_only_fixture(rng)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
+
+
+def quant_only_heads(rng: np.random.Generator) -> np.ndarray:
+    """Two benchmark heads plus the edge cases the kernels special-case."""
+    heads = [benchmark_head(rng), benchmark_head(rng)]
+    heads.append(np.zeros((128, 128), np.float32))                       # all zero
+    holes = benchmark_head(rng)
+    holes[:, 3] = 0.0
+    holes[9, :] = 0.0
+    holes[50, 60] = -7.5                                                 # lone outlier
+    heads.append(holes)
+    heads.append((rng.standard_normal((128, 128)) * 1e-41).astype(np.float32))  # denormals
+    wide = rng.standard_normal((128, 128)) * 10.0 ** rng.uniform(-30, 30, (128, 128))
+    heads.append(wide.astype(np.float32))                                # wild range
+    base = ((np.arange(128) % 127) + 0.5) * 2.0 ** -7                    # rounding ties
+    base = base * (0.25 / base.mean())
+    ties = np.stack([np.roll(base, k) for k in range(128)]).astype(np.float32)
+    ties *= np.where(rng.random((128, 128)) < 0.5, -1, 1).astype(np.float32)
+    heads.append(ties)
+    heads.append((rng.integers(-127, 128, (128, 128)) * 2.0 ** -9).astype(np.float32))
+    return np.stack(heads)
+
+
+def quant_only_fixture(rng: np.random.Generator) -> None:
+    if not oracle.ref_quant_available():
+        raise SystemExit("build the reference first: make -C oracle ref")
+    states = quant_only_heads(rng)
+    codes, smoothing, scales = oracle.ref_quant_encode(states)
+    dense = oracle.ref_quant_decode(codes, smoothing, scales)
+    queries = np.stack([unit_query(rng) for _ in range(states.shape[0])])
+    projection = oracle.ref_quant_project(codes, smoothing, scales, queries)
+    np.savez_compressed(OUT / "reference_quant_only.npz", states=states, codes=codes,
+                        smoothing=smoothing, scales=scales, dense=dense, query=queries,
+                        projection=projection)
 
 
 if __name__ == "__main__":

@@ -1,6 +1,6 @@
 """GPU parity: the sm_100a kernels, called through the C ABI, against the CPU
 oracle (oracle/gdn_codec_oracle.c, pinned to the reference library by
-tests/test_oracle_golden.py) and against the reference's own golden vectors.
+tests/test_oracle.py) and against the reference's own golden vectors.
 
 Bar: int8 codes, smoothing, scales and slot
 indexing bit-exact; dequantised values and projection outputs within
@@ -109,8 +109,8 @@ def test_encoded_projection(batch, layout):
                           to_np(q.float()).reshape(-1, 128), layout=layout, threads=8)
     got = to_np(out).reshape(-1, 128)
     assert_close_and_exact("projection", got, want)
-    # Fused readout equals dequantize-then-matvec within the fp32 tolerance
-    # against an fp64 recomputation (survey c4: record the fp64 error too).
+    # The fused readout also equals dequantize-then-matvec computed in fp64,
+    # within the fp32 tolerance.
     dense = to_np(codec.dequantize(enc)).reshape(-1, 128, 128).astype(np.float64)
     qd = to_np(q.float()).reshape(-1, 128).astype(np.float64)
     ref64 = (np.einsum("hkv,hk->hv", dense, qd) if layout == "capsule"
@@ -140,6 +140,30 @@ def test_reference_golden_vectors(golden):
     assert_bit_exact("scales", to_np(enc.scales), g["scales"])
     assert_close_and_exact("DenseState", to_np(dense), g["dense_state"])
     assert_close_and_exact("ApplyToken readout", to_np(proj), g["projection"])
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_reference_quant_only_fixture(golden, layout):
+    """Kernels against the reference's own quant-only code (QuantizeBoundary,
+    DequantizeBoundary and ReadWindowState of capsule.cpp at compensator
+    rank 0) on benchmark heads and edge cases; provider layout runs on the
+    transposed heads and must give the transposed results."""
+    g = golden["quant_only"]
+    provider = layout == "provider"
+    flip = (lambda a: np.ascontiguousarray(a.transpose(0, 2, 1))) if provider else (lambda a: a)
+    states = torch.from_numpy(flip(g["states"])).to(DEV)
+    enc = codec.quantize(states, layout)
+    dense = codec.dequantize(enc)
+    q = torch.from_numpy(g["query"]).to(DEV).to(torch.bfloat16)
+    assert torch.equal(q.float().cpu(), torch.from_numpy(g["query"]))  # bf16-exact queries
+    proj = codec.encoded_projection(enc, q)
+    torch.cuda.synchronize()
+    assert_bit_exact("codes", to_np(enc.codes), flip(g["codes"]))
+    assert_bit_exact("smoothing", to_np(enc.smoothing), g["smoothing"])
+    assert_bit_exact("scales", to_np(enc.scales), g["scales"])
+    assert_close_and_exact("dense", to_np(dense), flip(g["dense"]))
+    assert_bit_exact("dense bits", to_np(dense), flip(g["dense"]))
+    assert_close_and_exact("projection", to_np(proj), g["projection"])
 
 
 def test_reference_single_head_entry_points(golden):
