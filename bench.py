@@ -12,8 +12,10 @@ Output: one JSON line on rank 0 with the device-timed value (inputs resident
 in HBM), an end-to-end value through the public API with host buffers (H2D of
 the states and D2H of the reconstruction inside the timed region), the
 roofline of the dominant kernel, the CPU baseline, clocks sampled during the
-timed region and the launch count.  ``--impl reference`` times the CPU
-restatement of the reference codec (oracle/) on all host cores instead.
+timed region and the launch count.  ``--impl reference`` times the
+reference's own CPU codec (its quant-only stage compiled from the reference
+sources into oracle/_ref, or the C restatement in oracle/ where that library
+is absent) on all host cores instead.
 """
 
 from __future__ import annotations
@@ -129,28 +131,51 @@ class ClockSampler:
         }
 
 
-def cpu_baseline(layout: str, target_seconds: float = 3.0) -> dict:
-    """The oracle (C restatement of the reference's quant-only codec,
-    capsule.cpp:190-251) on all host cores over a bounded sample."""
+def cpu_codec(layout: str, cores: int):
+    """The CPU implementation timed beside the GPU: the reference's own
+    quant-only stage (QuantizeBoundary / DequantizeBoundary of capsule.cpp at
+    compensator rank 0, compiled from the reference sources into
+    oracle/_ref/libgdn_ref_quant.so) when it was built, for the capsule layout
+    it implements; otherwise the C restatement (oracle/gdn_codec_oracle.c).
+    Returns (kind, name, step) where step(states) runs quantize+dequantize."""
+    import oracle as oracle_mod  # noqa: PLC0415 - checker/baseline only, never the GPU path
+
+    if layout == "capsule" and oracle_mod.ref_quant_available():
+        def step(states):
+            z, c, b = oracle_mod.ref_quant_encode(states, threads=cores)
+            oracle_mod.ref_quant_decode(z, c, b, threads=cores)
+        return "reference", "oracle/_ref/libgdn_ref_quant.so (reference capsule.cpp)", step
+
+    def step(states):  # noqa: F811
+        z, c, b = oracle_mod.quantize(states, layout, threads=cores)
+        oracle_mod.dequantize(z, c, b, layout=layout, threads=cores)
+    return "port", "oracle/gdn_codec_oracle.c", step
+
+
+def sample_states(layout: str, heads: int):
+    """Seeded host heads of the benchmark distribution (per-head
+    log-uniform scale in [1e-3, 1], 1% zeros)."""
     import numpy as np
 
-    import oracle as oracle_mod  # noqa: PLC0415 - checker only, CPU leg of the bench
-
-    cores = os.cpu_count() or 1
     rng = np.random.default_rng(0)
-    sample_heads = 2048
-    scale = (10.0 ** (-3.0 * rng.random((sample_heads, 1, 1)))).astype(np.float32)
-    states = (rng.standard_normal((sample_heads, 128, 128), dtype=np.float32) * scale)
+    scale = (10.0 ** (-3.0 * rng.random((heads, 1, 1)))).astype(np.float32)
+    states = rng.standard_normal((heads, 128, 128), dtype=np.float32) * scale
     states[rng.random(states.shape) < 0.01] = 0.0
     if layout == "provider":
         states = np.ascontiguousarray(states.transpose(0, 2, 1))
-    # warm-up pass, then repeat until the time budget is used
-    z, c, b = oracle_mod.quantize(states, layout, threads=cores)
-    oracle_mod.dequantize(z, c, b, layout=layout, threads=cores)
+    return states
+
+
+def cpu_baseline(layout: str, target_seconds: float = 3.0) -> dict:
+    """The CPU codec on all host cores over a bounded sample (rank 0, N=1)."""
+    cores = os.cpu_count() or 1
+    sample_heads = 2048
+    states = sample_states(layout, sample_heads)
+    kind, name, step = cpu_codec(layout, cores)
+    step(states)  # warm-up pass, then repeat until the time budget is used
     passes, start = 0, time.perf_counter()
     while True:
-        z, c, b = oracle_mod.quantize(states, layout, threads=cores)
-        oracle_mod.dequantize(z, c, b, layout=layout, threads=cores)
+        step(states)
         passes += 1
         elapsed = time.perf_counter() - start
         if elapsed >= target_seconds:
@@ -159,46 +184,33 @@ def cpu_baseline(layout: str, target_seconds: float = 3.0) -> dict:
         "value": passes * sample_heads / elapsed,
         "unit": UNIT,
         "cores": cores,
-        "kind": "port",
+        "kind": kind,
         "sample": (f"{passes} passes of quantize+dequantize over {sample_heads} heads of the "
-                   f"benchmark distribution ({layout} layout), oracle/gdn_codec_oracle.c on "
-                   f"{cores} threads, {elapsed:.2f} s wall"),
+                   f"benchmark distribution ({layout} layout), {name} on {cores} threads, "
+                   f"{elapsed:.2f} s wall"),
     }
 
 
 def run_reference(args) -> None:
-    """--impl reference: the reference's CPU codec path (the oracle's C
-    restatement of native/src quant-only arithmetic) on all host cores."""
+    """--impl reference: the reference's CPU codec path on all host cores,
+    each step a bounded sample of the batched workload."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
-
-    import oracle as oracle_mod  # noqa: PLC0415
-
     cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
     sample_heads = 4096
-    scale = (10.0 ** (-3.0 * rng.random((sample_heads, 1, 1)))).astype(np.float32)
-    states = rng.standard_normal((sample_heads, 128, 128), dtype=np.float32) * scale
-    states[rng.random(states.shape) < 0.01] = 0.0
-    if args.layout == "provider":
-        states = np.ascontiguousarray(states.transpose(0, 2, 1))
-
-    def step():
-        z, c, b = oracle_mod.quantize(states, args.layout, threads=cores)
-        oracle_mod.dequantize(z, c, b, layout=args.layout, threads=cores)
-
+    states = sample_states(args.layout, sample_heads)
+    kind, name, step = cpu_codec(args.layout, cores)
     for _ in range(max(args.warmup, 0)):
-        step()
+        step(states)
     start = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        step(states)
     elapsed = time.perf_counter() - start
     value = args.steps * sample_heads / elapsed
     sample = (f"each step: quantize+dequantize of {sample_heads} heads of the benchmark "
-              f"distribution (a bounded sample of config 2's 61,440 heads per GPU), "
-              f"oracle/gdn_codec_oracle.c on {cores} threads")
+              f"distribution (a bounded sample of the 61,440 heads per GPU), {name} on "
+              f"{cores} threads")
     print(json.dumps({
         "impl": "reference",
         "metric": METRIC, "value": value, "unit": UNIT, "higher_is_better": True,
@@ -207,7 +219,7 @@ def run_reference(args) -> None:
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": "config2 sample: quantize+dequantize, CPU", "layout": args.layout,
                    "heads_per_step": sample_heads},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
