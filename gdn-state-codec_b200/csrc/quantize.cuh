@@ -151,17 +151,6 @@ __device__ __forceinline__ bool approx_ambiguous(float s, float km) {
   return !(fabsf(d) <= kAmbiguous);
 }
 
-// Exact codes for the elements of one 4-element chunk that lie inside the
-// ambiguity band (s exact; b exact maximum; km = RN(127 / b)).
-__device__ __forceinline__ void patch_chunk(int8_t* dst, float4 s, float4 km, float4 b) {
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    if (comp(km, e) != 0.0F && approx_ambiguous(comp(s, e), comp(km, e))) {
-      dst[e] = exact_code(comp(s, e), comp(b, e));
-    }
-  }
-}
-
 // Next work item at or after `item` (stride `step`) that names a real head.
 __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t item,
                                               uint64_t step, int64_t* head, bool report_bad) {
@@ -189,6 +178,134 @@ __device__ __forceinline__ void issue_head(const QuantizeParams& p, QuantizeGrou
 
 __device__ __forceinline__ float state_at(const QuantizeParams& p, int64_t head, int row, int col) {
   return __ldg(p.state + static_cast<uint64_t>(head) * kElements + row * 128 + col);
+}
+
+// ---------------------------------------------------------------------------
+// Cold paths, kept out of line so the hot per-head code stays compact (they
+// run for a small fraction of heads and re-read their inputs from global
+// memory instead of holding extra registers).
+
+// Sequential re-sum, in the reference's order (capsule.cpp:193-196: value
+// 0..127), of the capsule rows whose double mean lies near a float rounding
+// midpoint.  `flagged` has one bit per owning lane pair (even lanes); lanes
+// of a flagged pair get the sequential sum, the others keep `sum`.
+__device__ __noinline__ double resum_capsule_rows(const float* head_state, int row_base,
+                                                  int lane, uint32_t flagged, double sum) {
+  while (flagged != 0u) {
+    const int owner = __ffs(flagged) - 1;
+    flagged &= flagged - 1u;
+    const int row = row_base + 4 * ((owner >> 1) & 3) + (owner >> 3);
+    const float4 mine = __ldg(reinterpret_cast<const float4*>(head_state + row * 128) + lane);
+    double seq = 0.0;
+    for (int src = 0; src < 32; ++src) {
+      seq += fabsf(__shfl_sync(0xffffffffu, mine.x, src));
+      seq += fabsf(__shfl_sync(0xffffffffu, mine.y, src));
+      seq += fabsf(__shfl_sync(0xffffffffu, mine.z, src));
+      seq += fabsf(__shfl_sync(0xffffffffu, mine.w, src));
+    }
+    if ((lane >> 1) == (owner >> 1)) sum = seq;
+  }
+  return sum;
+}
+
+// Exact codes for a capsule thread's 4-element chunks flagged in `mask` (bit
+// 4c + j: row 16w + 4j + g, columns 32c + 4q ..): s = R / c by IEEE division
+// (equal to the kernel's exact quotient), then the reference's code.  Values
+// on the IEEE path (km == 0) are left to slow_capsule_values.
+__device__ __noinline__ void patch_capsule_codes(const float* head_state, int8_t* codes,
+                                                 const float* key_c, const float* val_b,
+                                                 const float* val_km, int row_base, int g, int q,
+                                                 uint32_t mask) {
+  while (mask != 0u) {
+    const int bit = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    const int r = row_base + 4 * (bit & 3) + g;
+    const float c = key_c[r];
+    for (int e = 0; e < 4; ++e) {
+      const int col = 32 * (bit >> 2) + 4 * q + e;
+      if (val_km[col] == 0.0F) continue;
+      codes[r * kValues + col] = exact_code(__fdiv_rn(__ldg(head_state + r * 128 + col), c), val_b[col]);
+    }
+  }
+}
+
+// IEEE path of a capsule head for values outside the fast ranges: exact
+// quotients from the input, exact maxima across the block, then codes and
+// scales.  Called by every thread of the block (contains block barriers).
+__device__ __noinline__ void slow_capsule_values(const float* head_state, int8_t* codes,
+                                                 float* scales, const float* key_c,
+                                                 const float* val_km, uint32_t* val_exact,
+                                                 int row_base, int g, int q, int gtid) {
+  for (int j = 0; j < 4; ++j) {
+    const int r = row_base + 4 * j + g;
+    for (int c = 0; c < 4; ++c) {
+      for (int e = 0; e < 4; ++e) {
+        const int col = 32 * c + 4 * q + e;
+        if (val_km[col] != 0.0F) continue;
+        const float x = __ldg(head_state + r * 128 + col);
+        if (x != 0.0F) atomicMax(&val_exact[col], __float_as_uint(fabsf(__fdiv_rn(x, key_c[r]))));
+      }
+    }
+  }
+  __syncthreads();
+  if (gtid < kValues && val_km[gtid] == 0.0F) scales[gtid] = __uint_as_float(val_exact[gtid]);
+  for (int j = 0; j < 4; ++j) {
+    const int r = row_base + 4 * j + g;
+    for (int c = 0; c < 4; ++c) {
+      for (int e = 0; e < 4; ++e) {
+        const int col = 32 * c + 4 * q + e;
+        if (val_km[col] != 0.0F) continue;
+        const float x = __ldg(head_state + r * 128 + col);
+        codes[r * kValues + col] =
+            exact_code(x == 0.0F ? 0.0F : __fdiv_rn(x, key_c[r]), __uint_as_float(val_exact[col]));
+      }
+    }
+  }
+}
+
+// Provider counterpart of patch_capsule_codes: rows v = row_base + j flagged
+// in `mask`, this lane's keys 4l .. 4l + 3.
+__device__ __noinline__ void patch_provider_codes(const float* head_state, int8_t* codes,
+                                                  const float* key_c, const float* val_b,
+                                                  const float* val_km, int row_base, int lane,
+                                                  uint32_t mask) {
+  while (mask != 0u) {
+    const int j = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    const int v = row_base + j;
+    const float km = val_km[v];
+    if (km == 0.0F) continue;
+    for (int e = 0; e < 4; ++e) {
+      const int k = 4 * lane + e;
+      codes[v * kKeys + k] = exact_code(__fdiv_rn(__ldg(head_state + v * 128 + k), key_c[k]), val_b[v]);
+    }
+  }
+}
+
+// Provider IEEE path for the value rows in `slow_rows` (bit 2j: row
+// row_base + j): exact quotients, the row maximum across the warp, codes.
+__device__ __noinline__ void slow_provider_rows(const float* head_state, int8_t* codes,
+                                                float* scales, float4 c4, int row_base, int lane,
+                                                uint32_t slow_rows) {
+  while (slow_rows != 0u) {
+    const int owner = __ffs(slow_rows) - 1;
+    slow_rows &= slow_rows - 1u;
+    const int j = owner >> 1;
+    const float4 r4 = __ldg(reinterpret_cast<const float4*>(head_state + (row_base + j) * 128) + lane);
+    float4 s4;
+    s4.x = r4.x == 0.0F ? 0.0F : __fdiv_rn(r4.x, c4.x);
+    s4.y = r4.y == 0.0F ? 0.0F : __fdiv_rn(r4.y, c4.y);
+    s4.z = r4.z == 0.0F ? 0.0F : __fdiv_rn(r4.z, c4.z);
+    s4.w = r4.w == 0.0F ? 0.0F : __fdiv_rn(r4.w, c4.w);
+    float mx = absmax4(s4);
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) scales[row_base + j] = mx;
+    const uint32_t word = (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.x, mx)))) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.y, mx))) << 8) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.z, mx))) << 16) |
+                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.w, mx))) << 24);
+    st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -245,25 +362,12 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
     double sum = part[0] + __shfl_xor_sync(0xffffffffu, part[0], 1);
     const int my_j = (lane >> 1) & 3;  // this lane pair's row r = 16w + 4*my_j + g
     // Rows whose float mean could depend on the summation order are re-summed
-    // in the reference's order (capsule.cpp:193-196): value 0..127, re-read
-    // from the input.  Rare.
-    uint32_t flagged =
+    // in the reference's order.  Rare.
+    const uint32_t flagged =
         __ballot_sync(0xffffffffu, near_float_midpoint(sum * (1.0 / 128.0))) & 0x55555555u;
-    while (flagged != 0u) {
-      const int owner = __ffs(flagged) - 1;
-      flagged &= flagged - 1u;
-      const int row = row_base + 4 * ((owner >> 1) & 3) + (owner >> 3);
-      const float4 mine = __ldg(reinterpret_cast<const float4*>(
-                                    p.state + static_cast<uint64_t>(head) * kElements + row * 128) +
-                                lane);
-      double seq = 0.0;
-      for (int src = 0; src < 32; ++src) {
-        seq += fabsf(__shfl_sync(0xffffffffu, mine.x, src));
-        seq += fabsf(__shfl_sync(0xffffffffu, mine.y, src));
-        seq += fabsf(__shfl_sync(0xffffffffu, mine.z, src));
-        seq += fabsf(__shfl_sync(0xffffffffu, mine.w, src));
-      }
-      if ((lane >> 1) == (owner >> 1)) sum = seq;
+    if (flagged != 0u) {
+      sum = resum_capsule_rows(p.state + static_cast<uint64_t>(head) * kElements, row_base, lane,
+                               flagged, sum);
     }
     const float c = smoothing_from_sum(sum);
     if ((lane & 1) == 0) {
@@ -331,59 +435,26 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
 
   // -- codes ----------------------------------------------------------------------
   int8_t* codes = p.codes + static_cast<uint64_t>(head) * kElements;
+  uint32_t amb_mask = 0u;  // bit 4c + j: chunk (j, c) holds an element near a boundary
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const float4 km = reinterpret_cast<const float4*>(gs.val_km)[8 * c + q];
-    uint32_t amb_rows = 0u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       bool amb;
       const uint32_t word = approx_codes(t.v[j][c], km, &amb);
       st_cs_u32(codes + (row_base + 4 * j + g) * kValues + 32 * c + 4 * q, word);
-      amb_rows |= (amb ? 1u : 0u) << j;
-    }
-    if (amb_rows != 0u) {  // rare: exact codes from the exact s
-      const float4 b = reinterpret_cast<const float4*>(gs.val_b)[8 * c + q];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if ((amb_rows >> j) & 1u) {
-          patch_chunk(codes + (row_base + 4 * j + g) * kValues + 32 * c + 4 * q, t.v[j][c], km, b);
-        }
-      }
+      amb_mask |= (amb ? 1u : 0u) << (4 * c + j);
     }
   }
-  if (any_slow) {
-    // IEEE path for values outside the fast ranges: exact quotients from the
-    // input, exact maxima across the group, then codes.  Rare.
-    for (int j = 0; j < 4; ++j) {
-      const int r = row_base + 4 * j + g;
-      for (int c = 0; c < 4; ++c) {
-        for (int e = 0; e < 4; ++e) {
-          const int col = 32 * c + 4 * q + e;
-          if (gs.val_km[col] != 0.0F) continue;
-          const float x = state_at(p, head, r, col);
-          if (x != 0.0F) {
-            atomicMax(&gs.val_exact[col], __float_as_uint(fabsf(__fdiv_rn(x, gs.key_c[r]))));
-          }
-        }
-      }
-    }
-    group_sync(group);
-    if (gtid < kValues && gs.val_km[gtid] == 0.0F) {
-      p.scales[head * kValues + gtid] = __uint_as_float(gs.val_exact[gtid]);
-    }
-    for (int j = 0; j < 4; ++j) {
-      const int r = row_base + 4 * j + g;
-      for (int c = 0; c < 4; ++c) {
-        for (int e = 0; e < 4; ++e) {
-          const int col = 32 * c + 4 * q + e;
-          if (gs.val_km[col] != 0.0F) continue;
-          const float x = state_at(p, head, r, col);
-          codes[r * kValues + col] = exact_code(x == 0.0F ? 0.0F : __fdiv_rn(x, gs.key_c[r]),
-                                                __uint_as_float(gs.val_exact[col]));
-        }
-      }
-    }
+  const float* head_state = p.state + static_cast<uint64_t>(head) * kElements;
+  if (amb_mask != 0u) {  // rare: exact codes by IEEE division
+    patch_capsule_codes(head_state, codes, gs.key_c, gs.val_b, gs.val_km, row_base, g, q,
+                        amb_mask);
+  }
+  if (any_slow) {  // rare and block-uniform: values outside the fast ranges
+    slow_capsule_values(head_state, codes, p.scales + head * kValues, gs.key_c, gs.val_km,
+                        gs.val_exact, row_base, g, q, gtid);
   }
 }
 
@@ -504,41 +575,15 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
     st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
     amb_rows |= (amb ? 1u : 0u) << j;
   }
-  if (amb_rows != 0u) {  // rare: exact codes from the exact s
-#pragma unroll
-    for (int j = 0; j < kWarpRows; ++j) {
-      if ((amb_rows >> j) & 1u) {
-        const float km = gs.val_km[row_base + j];
-        const float bb = gs.val_b[row_base + j];
-        patch_chunk(codes + (row_base + j) * kKeys + 4 * lane, v[j], make_float4(km, km, km, km),
-                    make_float4(bb, bb, bb, bb));
-      }
-    }
+  const float* head_state = p.state + static_cast<uint64_t>(head) * kElements;
+  if (amb_rows != 0u) {  // rare: exact codes by IEEE division
+    patch_provider_codes(head_state, codes, gs.key_c, gs.val_b, gs.val_km, row_base, lane,
+                         amb_rows);
   }
   // IEEE path for rows outside the fast ranges (rare; all-zero rows included).
-  uint32_t slow_left = slow_rows;
-  while (slow_left != 0u) {
-    const int owner = __ffs(slow_left) - 1;
-    slow_left &= slow_left - 1u;
-    const int j = owner >> 1;
-    const float4 r4 = __ldg(reinterpret_cast<const float4*>(
-                                p.state + static_cast<uint64_t>(head) * kElements +
-                                (row_base + j) * 128) +
-                            lane);
-    float4 s4;
-    s4.x = r4.x == 0.0F ? 0.0F : __fdiv_rn(r4.x, c4.x);
-    s4.y = r4.y == 0.0F ? 0.0F : __fdiv_rn(r4.y, c4.y);
-    s4.z = r4.z == 0.0F ? 0.0F : __fdiv_rn(r4.z, c4.z);
-    s4.w = r4.w == 0.0F ? 0.0F : __fdiv_rn(r4.w, c4.w);
-    float mx = absmax4(s4);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (lane == 0) p.scales[head * kValues + row_base + j] = mx;
-    const uint32_t word = (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.x, mx)))) |
-                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.y, mx))) << 8) |
-                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.z, mx))) << 16) |
-                          (static_cast<uint32_t>(static_cast<uint8_t>(exact_code(s4.w, mx))) << 24);
-    st_cs_u32(codes + (row_base + j) * kKeys + 4 * lane, word);
+  if (slow_rows != 0u) {
+    slow_provider_rows(head_state, codes, p.scales + head * kValues, c4, row_base, lane,
+                       slow_rows);
   }
 }
 
