@@ -23,7 +23,7 @@
 //    RN(1/c) by two packed fma corrections (div4_exact), so the per-value
 //    maxima b are exact without any search; codes come from one multiply by
 //    RN(127 / b), and the few elements within the proven error band of a
-//    rounding boundary take the exact code from the exact s.
+//    rounding boundary take the exact code by IEEE division (out of line).
 //  * thread tiles (64 elements per thread) keep the double-precision
 //    reduction mostly inside a thread: capsule layout (row sums over values)
 //    uses 4 rows x 16 columns, provider layout (column sums over values)
@@ -39,11 +39,13 @@ constexpr int kQBlocksPerSm = 2;                    // independent head streams 
 constexpr int kGroupWarps = kQThreads / 32;         // 8
 constexpr int kWarpRows = kKeys / kGroupWarps;      // 16 rows of a head per warp
 
-// Codes: t' = RN(s * RN(127 / b)) and the exact t = RN(RN(s / b) * 127) both
-// lie within 2^-23 (relative, two roundings each) of s * 127 / b, so
-// |t' - t| <= 127 * 2^-22 < 2^-15: a code is decided from t' unless t' lies
-// within 2^-13 of a rounding boundary n + 0.5.
-constexpr float kAmbiguous = 0.5F - 0x1p-13F;
+// Codes: with km = RN(127 / b) = (127 / b)(1 + e1), the approximation
+// t' = RN(s * km) = T (1 + e1)(1 + e2) and the reference's
+// t = RN(RN(s / b) * 127) = T (1 + e3)(1 + e4) of T = 127 s / b, |T| <= 127,
+// |e_i| <= 2^-24, differ by at most 127 * 2^-22 * (1 + 2^-24) < 2^-15.  A code
+// is therefore decided from t' unless t' lies within 2^-15 of a rounding
+// boundary n + 0.5 (ties of t included); those elements take the exact code.
+constexpr float kAmbiguous = 0.5F - 0x1p-15F;
 // Fast-path ranges: a per-value maximum b in [2^-64, 2^100] and smoothing in
 // [2^-14, 2^100] keep every element that can be a maximum or have a nonzero
 // code (|s| >= b / 254) inside div4_exact's preconditions (|R| >= 2^-102,
@@ -85,7 +87,9 @@ struct __align__(128) QuantizeGroupShared {
   uint32_t val_exact[kValues];         // IEEE path: maximum (bits)
   float colbuf[kKeys];                 // provider: one column for a sequential re-sum
   int col_flag[kKeys];
-  uint64_t full;                       // mbarrier of the landing buffer
+  uint64_t full;                       // landing buffer holds the next head (TMA bytes)
+  uint64_t empty;                      // provider: every warp has copied the head
+  int readers;                         // capsule: warps that have copied the current head
 };
 
 // Block-wide barriers (the CTA is one head stream).
@@ -95,9 +99,6 @@ __device__ __forceinline__ bool group_sync_or(int, bool pred) { return __syncthr
 // ---------------------------------------------------------------------------
 // Small helpers.
 
-__device__ __forceinline__ float comp(const float4& a, int i) {
-  return i == 0 ? a.x : (i == 1 ? a.y : (i == 2 ? a.z : a.w));
-}
 __device__ __forceinline__ double abs_sum4(float4 a) {
   return (static_cast<double>(fabsf(a.x)) + static_cast<double>(fabsf(a.y))) +
          (static_cast<double>(fabsf(a.z)) + static_cast<double>(fabsf(a.w)));
@@ -221,10 +222,15 @@ __device__ __noinline__ void patch_capsule_codes(const float* head_state, int8_t
     mask &= mask - 1u;
     const int r = row_base + 4 * (bit & 3) + g;
     const float c = key_c[r];
+    const int col0 = 32 * (bit >> 2) + 4 * q;
+    const float4 r4 = __ldg(reinterpret_cast<const float4*>(head_state + r * 128 + col0));
+    const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
     for (int e = 0; e < 4; ++e) {
-      const int col = 32 * (bit >> 2) + 4 * q + e;
-      if (val_km[col] == 0.0F) continue;
-      codes[r * kValues + col] = exact_code(__fdiv_rn(__ldg(head_state + r * 128 + col), c), val_b[col]);
+      const int col = col0 + e;
+      const float km = val_km[col];
+      if (km == 0.0F) continue;
+      const float s = __fdiv_rn(rv[e], c);
+      if (approx_ambiguous(s, km)) codes[r * kValues + col] = exact_code(s, val_b[col]);
     }
   }
 }
@@ -275,9 +281,12 @@ __device__ __noinline__ void patch_provider_codes(const float* head_state, int8_
     const int v = row_base + j;
     const float km = val_km[v];
     if (km == 0.0F) continue;
+    const float4 r4 = __ldg(reinterpret_cast<const float4*>(head_state + v * 128) + lane);
+    const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
     for (int e = 0; e < 4; ++e) {
       const int k = 4 * lane + e;
-      codes[v * kKeys + k] = exact_code(__fdiv_rn(__ldg(head_state + v * 128 + k), key_c[k]), val_b[v]);
+      const float s = __fdiv_rn(rv[e], key_c[k]);
+      if (approx_ambiguous(s, km)) codes[v * kKeys + k] = exact_code(s, val_b[v]);
     }
   }
 }
@@ -324,10 +333,10 @@ struct CapsuleTile {
 };
 
 template <int kMode>
-__device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
+__device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p,
                                                       QuantizeGroupShared& gs, CapsuleTile& t,
                                                       int64_t head, int group, int warp, int lane,
-                                                      int gtid) {
+                                                      int gtid, bool timed_out) {
   const int g = lane >> 3, q = lane & 7;
   const int row_base = warp * kWarpRows;
   // -- smoothing per row -----------------------------------------------------
@@ -378,7 +387,7 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
     }
   }
   __syncwarp();
-  if (kMode == kSmoothingOnly) return;
+  if (kMode == kSmoothingOnly) return group_sync_or(group, timed_out);
 
   // -- exact smoothed values and column maxima ------------------------------------
 #pragma unroll
@@ -410,7 +419,9 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
     const float4 keep = up ? red[1] : red[0];
     reinterpret_cast<float4*>(gs.col_part[warp])[8 * g + q] = fmax4(keep, shfl_xor4(send, 8));
   }
-  group_sync(group);  // B1: column partial maxima and smoothing published
+  // B1: column partial maxima and smoothing published; a bounded wait that
+  // expired anywhere in the block ends the launch (uniform result).
+  if (group_sync_or(group, timed_out)) return true;
   bool slow = false;
   if (gtid < kValues) {
     // Caller-given smoothing out of the fast range sends the whole head to
@@ -456,6 +467,7 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
     slow_capsule_values(head_state, codes, p.scales + head * kValues, gs.key_c, gs.val_km,
                         gs.val_exact, row_base, g, q, gtid);
   }
+  return false;
 }
 
 // ---------------------------------------------------------------------------
@@ -464,10 +476,11 @@ __device__ __forceinline__ void quantize_capsule_head(const QuantizeParams& p,
 // (a warp reads one 512-byte row per instruction: conflict-free).
 
 template <int kMode>
-__device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
+__device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
                                                        QuantizeGroupShared& gs,
                                                        float4 (&v)[kWarpRows], int64_t head,
-                                                       int group, int warp, int lane, int gtid) {
+                                                       int group, int warp, int lane, int gtid,
+                                                       bool timed_out) {
   const int row_base = warp * kWarpRows;
   // -- smoothing per key (column): thread-local over 16 rows, then across warps
   if (kMode != kGivenSmoothing) {
@@ -485,7 +498,9 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
     dst[2] = cs2;
     dst[3] = cs3;
   }
-  group_sync(group);  // B1: column partial sums published
+  // B1: column partial sums published; a bounded wait that expired anywhere
+  // in the block ends the launch (uniform result).
+  if (group_sync_or(group, timed_out)) return true;
   int flag = 0;
   bool bad_smoothing = false;
   if (gtid < kKeys) {
@@ -527,7 +542,7 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
       group_sync(group);
     }
   }
-  if (kMode == kSmoothingOnly) return;
+  if (kMode == kSmoothingOnly) return false;
 
   // -- exact smoothed values and row maxima (warp-local) ------------------------------
   const float4 c4 = reinterpret_cast<const float4*>(gs.key_c)[lane];
@@ -585,6 +600,7 @@ __device__ __forceinline__ void quantize_provider_head(const QuantizeParams& p,
     slow_provider_rows(head_state, codes, p.scales + head * kValues, c4, row_base, lane,
                        slow_rows);
   }
+  return false;
 }
 
 // ---------------------------------------------------------------------------
@@ -603,17 +619,27 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
 
   if (gtid == 0) {
     mbar_init(&gs.full, 1);
+    mbar_init(&gs.empty, kGroupWarps);
+    gs.readers = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
+  // The landing buffer cycles full -> (every warp copies it) -> refill, and
+  // warps never wait for one another there.  Two release schemes, chosen per
+  // layout by measurement: the provider kernel has every warp arrive on the
+  // `empty` mbarrier and thread 0 wait on it before issuing the next head;
+  // the capsule kernel counts copies in shared memory and the last warp to
+  // finish issues the next head itself (the count is reset before that
+  // warp's arrive.expect_tx, whose release the other warps acquire through
+  // the `full` barrier before they count again).  The block barriers inside
+  // the head (B1, B2) order every other shared array between heads.
   int64_t head = -1;
   uint64_t item = next_item(p, first, step, &head, gtid == 0);
   if (gtid == 0 && head >= 0) issue_head(p, gs, head);
   uint32_t parity = 0;
   while (head >= 0) {
-    const bool timed_out = !mbar_wait_bounded(&gs.full, parity);
-    parity ^= 1u;
+    bool timed_out = !mbar_wait_bounded(&gs.full, parity);
     CapsuleTile ct;
     float4 pv[kWarpRows];
     if (kProvider) {
@@ -630,24 +656,54 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
         for (int c = 0; c < 4; ++c) ct.v[j][c] = src[row * 32 + 8 * c + q];
       }
     }
+    __syncwarp();
     int64_t next_head = -1;
     const uint64_t next = next_item(p, item + step, step, &next_head, gtid == 0);
-    // B0: the group holds this head in registers; the buffer takes the next.
-    if (group_sync_or(group, timed_out)) {
-      // A bounded wait expired: report it and let the copy in flight land
-      // (again bounded) so no bulk copy targets this block after it exits.
-      // Outputs of this launch are then unspecified.
+    bool issued = false;
+    if (kProvider) {
+      // Every warp arrives on `empty`; thread 0 waits for all of them, then
+      // issues the next head.
+      if (lane == 0) mbar_arrive(&gs.empty);
+      if (gtid == 0 && next_head >= 0) {
+        if (mbar_wait_bounded(&gs.empty, parity)) {
+          issue_head(p, gs, next_head);
+          issued = true;
+        } else {
+          timed_out = true;
+        }
+      }
+    } else {
+      // The last warp to finish copying issues the next head; nobody waits.
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();  // this warp's reads of the buffer precede its count
+        last = atomicAdd(&gs.readers, 1) == kGroupWarps - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last && lane == 0) {
+        gs.readers = 0;
+        if (next_head >= 0) {
+          issue_head(p, gs, next_head);
+          issued = true;
+        }
+      }
+    }
+    parity ^= 1u;
+    // The head functions fold `timed_out` into their first block barrier and
+    // return the block-wide result.
+    const bool abort =
+        kProvider ? quantize_provider_head<kMode>(p, gs, pv, head, group, warp, lane, gtid, timed_out)
+                  : quantize_capsule_head<kMode>(p, gs, ct, head, group, warp, lane, gtid, timed_out);
+    if (abort) {
+      // A bounded wait expired somewhere in the block: report it, let a copy
+      // still in flight land (again bounded) so that no bulk copy targets this
+      // block after it exits, and stop.  Outputs of this launch are then
+      // unspecified.
       if (gtid == 0) {
         report(p.status, kStatusWaitTimeout);
-        if (timed_out) (void)mbar_wait_bounded(&gs.full, parity ^ 1u);
+        if (issued) (void)mbar_wait_bounded(&gs.full, parity);
       }
       return;
-    }
-    if (gtid == 0 && next_head >= 0) issue_head(p, gs, next_head);
-    if (kProvider) {
-      quantize_provider_head<kMode>(p, gs, pv, head, group, warp, lane, gtid);
-    } else {
-      quantize_capsule_head<kMode>(p, gs, ct, head, group, warp, lane, gtid);
     }
     item = next;
     head = next_head;
