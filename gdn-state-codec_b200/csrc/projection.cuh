@@ -14,7 +14,8 @@
 // each lane four outputs v = 4l..4l+3, so the sequential k-sum is four
 // independent fp32 chains per lane (two packed fp32x2 chains).
 //  * capsule codes [k][v]: at step k a warp reads one 128-byte code row;
-//    16 rows are kept in flight per lane.
+//    the loads of the next batch of 8 rows are in flight while the current
+//    batch is accumulated (software pipelining).
 //  * provider codes [v][k]: a lane's four outputs are four code rows, so the
 //    warp loads its 16 KiB head with coalesced 128-bit loads, stores it to
 //    shared memory with an XOR swizzle on 16-byte chunks and reads its rows
@@ -27,6 +28,7 @@ namespace gdnsc {
 
 constexpr int kPThreads = 128;
 constexpr int kPWarps = kPThreads / 32;
+constexpr int kPBatch = 8;   // capsule code rows per pipelined batch
 
 struct ProjectParams {
   const int8_t* codes;              // [heads][128][128]
@@ -160,25 +162,44 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
     f2 kp01 = pack2(0.F, 0.F), kp23 = pack2(0.F, 0.F);
     const f2 magic = pack2(kCodeMagic, kCodeMagic);
     if (!kProvider) {
+      // Software-pipelined over batches of kPBatch code rows: the loads of the
+      // next batch are in flight while this batch is accumulated.
       const uint32_t* cw = reinterpret_cast<const uint32_t*>(codes) + lane;
-#pragma unroll 1
-      for (int k0 = 0; k0 < kKeys; k0 += 16) {
-        uint32_t w[16];
+      const float4* cx2 = reinterpret_cast<const float4*>(sh.cx[warp]);  // rows k, k + 1
+      auto rows = [&](const uint32_t (&w)[kPBatch], int k) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = ld_cs_u32(cw + (k0 + i) * 32);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 cx = sh.cx[warp][k0 + i];
+        for (int i = 0; i < kPBatch; i += 2) {
+          const float4 cc = cx2[(k + i) >> 1];
           f2 z01, z23;
           unpack_codes(w[i], z01, z23);
-          accumulate(a01, a23, z01, z23, cx.x, cx.y);
+          accumulate(a01, a23, z01, z23, cc.x, cc.y);
+          unpack_codes(w[i + 1], z01, z23);
+          accumulate(a01, a23, z01, z23, cc.z, cc.w);
           if (kCompensated) {
-            const float4 kk = sh.kr[warp][k0 + i];
-            const f2 xx = pack2(cx.y, cx.y);
-            kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
-            kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float4 kk = sh.kr[warp][k + i + h];
+              const float x = h == 0 ? cc.y : cc.w;
+              const f2 xx = pack2(x, x);
+              kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
+              kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
+            }
           }
         }
+      };
+      uint32_t wa[kPBatch], wb[kPBatch];
+#pragma unroll
+      for (int i = 0; i < kPBatch; ++i) wa[i] = ld_cs_u32(cw + i * 32);
+#pragma unroll 1
+      for (int k0 = 0; k0 < kKeys; k0 += 2 * kPBatch) {
+#pragma unroll
+        for (int i = 0; i < kPBatch; ++i) wb[i] = ld_cs_u32(cw + (k0 + kPBatch + i) * 32);
+        rows(wa, k0);
+        if (k0 + 2 * kPBatch < kKeys) {
+#pragma unroll
+          for (int i = 0; i < kPBatch; ++i) wa[i] = ld_cs_u32(cw + (k0 + 2 * kPBatch + i) * 32);
+        }
+        rows(wb, k0 + kPBatch);
       }
     } else {
       // Lane owns rows v = 4l + j; rows j = 0,1 form pair 01, rows 2,3 pair 23.
