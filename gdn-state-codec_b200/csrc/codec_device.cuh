@@ -282,6 +282,22 @@ __device__ __forceinline__ uint4 ld_cs_v4u(const void* p) {
   return __ldcs(reinterpret_cast<const uint4*>(p));
 }
 
+// Asynchronous 16-byte global -> shared copies (cp.async, cached in L2 only),
+// grouped per thread with commit / wait_group.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's committed groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // --------------------------------------------------------------------------
 // Slot-indexed work lists.  A work item is (batch entry, head within slot).
 // slot_ids == nullptr means item i is head i of a dense batch.

@@ -45,8 +45,25 @@ struct ProjectParams {
 
 struct ProjectShared {
   float2 cx[kPWarps][kKeys];        // (c_k, x_k) per warp
-  float4 kr[kPWarps][kKeys];        // compensator keys per warp
-  uint4 codes[kPWarps][kElements / 16];  // provider: staged head (swizzled)
+  float4 kr[kPWarps][kKeys];        // compensator keys per warp (full format only)
+};
+
+// Provider codes are streamed through shared memory in key slabs: slab s of a
+// head holds keys 32s .. 32s + 31 of all 128 value rows (4 KiB).  Each warp
+// owns a ring of kSlabStages slabs filled by cp.async, so the copies of the
+// next slabs (of this head or the next) overlap the current slab's arithmetic.
+// Within a slab, the 32 bytes of rows 4L .. 4L + 3 form line L (128 bytes,
+// eight 16-byte chunks c = 2 * (row % 4) + half) and chunk c is stored at
+// position c ^ (L % 8), so a lane reading its own four rows hits eight
+// distinct bank groups per quarter warp.
+constexpr int kSlabKeys = 32;
+constexpr int kSlabsPerHead = kKeys / kSlabKeys;           // 4
+constexpr int kSlabStages = 3;
+constexpr int kSlabChunks = kValues * kSlabKeys / 16;      // 256 x 16 bytes
+struct ProviderProjectShared {
+  uint4 slab[kPWarps][kSlabStages][kSlabChunks];
+  float4 cx[kPWarps][kKeys / 2];    // (c_k, x_k, c_k+1, x_k+1) per warp
+  float4 kr[kPWarps][kKeys];        // compensator keys per warp (full format only)
 };
 
 __device__ __forceinline__ float4 bf16x4_to_float4(uint2 w) {
@@ -100,7 +117,8 @@ __device__ __forceinline__ float4 finish_outputs(f2 a01, f2 a23, float4 b4, bool
   return make_float4(lo2(o01), hi2(o01), lo2(o23), hi2(o23));
 }
 
-template <bool kProvider, bool kCompensated>
+// Capsule codes [k][v].
+template <bool kCompensated>
 __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ProjectShared& sh = *reinterpret_cast<ProjectShared*>(smem_raw);
@@ -119,12 +137,6 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
     }
     const uint64_t hbase = static_cast<uint64_t>(head);
     const int8_t* codes = p.codes + hbase * kElements;
-    // Provider codes: issue the first half of the head's coalesced loads.
-    uint4 staged[kProvider ? 16 : 1];
-    if (kProvider) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) staged[i] = ld_cs_v4u(codes + i * 512 + 16 * lane);
-    }
     // (c_k, x_k) and compensator keys for this head into this warp's slots.
     const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.smoothing + hbase * kKeys) + lane);
     const float4 x4 = bf16x4_to_float4(
@@ -137,31 +149,11 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) sh.kr[warp][4 * lane + i] = __ldg(kp + 4 * lane + i);
     }
-    if (kProvider) {
-      // Load i covers row r = 4i + lane/8, chunk lane%8; it is stored at the
-      // swizzled chunk (lane%8) ^ (r/4 % 8) so that a lane reading its own
-      // rows (r/4 == lane) hits eight distinct bank groups per quarter warp.
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (half == 1) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) staged[i] = ld_cs_v4u(codes + (16 + i) * 512 + 16 * lane);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int li = 16 * half + i;
-          const int row = 4 * li + (lane >> 3);
-          const int chunk = (lane & 7) ^ (li & 7);
-          sh.codes[warp][row * 8 + chunk] = staged[i];
-        }
-      }
-    }
     __syncwarp();
 
     f2 a01 = pack2(0.F, 0.F), a23 = pack2(0.F, 0.F);
     f2 kp01 = pack2(0.F, 0.F), kp23 = pack2(0.F, 0.F);
-    const f2 magic = pack2(kCodeMagic, kCodeMagic);
-    if (!kProvider) {
+    {
       // Software-pipelined over batches of kPBatch code rows: the loads of the
       // next batch are in flight while this batch is accumulated.
       const uint32_t* cw = reinterpret_cast<const uint32_t*>(codes) + lane;
@@ -201,36 +193,6 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
         }
         rows(wb, k0 + kPBatch);
       }
-    } else {
-      // Lane owns rows v = 4l + j; rows j = 0,1 form pair 01, rows 2,3 pair 23.
-      const int swz = lane & 7;  // (row >> 2) & 7 for all four rows
-#pragma unroll 1
-      for (int chunk = 0; chunk < 8; ++chunk) {
-        uint4 r[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = sh.codes[warp][(4 * lane + j) * 8 + (chunk ^ swz)];
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const uint32_t b0 = reinterpret_cast<const uint32_t*>(&r[0])[wi] ^ kCodeBias;
-          const uint32_t b1 = reinterpret_cast<const uint32_t*>(&r[1])[wi] ^ kCodeBias;
-          const uint32_t b2 = reinterpret_cast<const uint32_t*>(&r[2])[wi] ^ kCodeBias;
-          const uint32_t b3 = reinterpret_cast<const uint32_t*>(&r[3])[wi] ^ kCodeBias;
-#pragma unroll
-          for (int byte = 0; byte < 4; ++byte) {
-            const int k = chunk * 16 + wi * 4 + byte;
-            const float2 cx = sh.cx[warp][k];
-            const f2 z01 = sub2(pack2(code_magic(b0, byte), code_magic(b1, byte)), magic);
-            const f2 z23 = sub2(pack2(code_magic(b2, byte), code_magic(b3, byte)), magic);
-            accumulate(a01, a23, z01, z23, cx.x, cx.y);
-            if (kCompensated) {
-              const float4 kk = sh.kr[warp][k];
-              const f2 xx = pack2(cx.y, cx.y);
-              kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
-              kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
-            }
-          }
-        }
-      }
     }
     const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.scales + hbase * kValues) + lane);
     // Every lane holds all four rank projections p_r (identical chains).
@@ -242,9 +204,161 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
   }
 }
 
-size_t project_smem_bytes(bool provider) {
-  return provider ? sizeof(ProjectShared)
-                  : offsetof(ProjectShared, codes);
+// Provider codes [v][k]: lane l owns outputs v = 4l .. 4l + 3 (rows of the
+// code matrix) and accumulates them over k = 0..127 in order, slab by slab.
+template <bool kCompensated>
+__global__ void __launch_bounds__(kPThreads) project_provider_kernel(ProjectParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  ProviderProjectShared& sh = *reinterpret_cast<ProviderProjectShared*>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kPWarps;
+  const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kPWarps + warp;
+  uint4* ring = sh.slab[warp][0];
+
+  // The warp streams (item, slab) positions in order; a position's slab sits
+  // in ring stage (position % kSlabStages).  Copies run kSlabStages - 1
+  // positions ahead of the arithmetic.
+  auto head_of = [&](uint64_t item) -> int64_t {
+    bool bad = false;
+    return item < p.items ? resolve_item(p.map, item, &bad) : -1;
+  };
+  // Lane-constant parts of the slab copy: piece lane + 32i is row
+  // 16i + lane/2, half lane%2, stored in line 4i + lane/8 at chunk
+  // (lane%8) ^ ((4i + lane/8) % 8) = (lane%8) ^ g ^ 4(i%2), g = lane/8.
+  const int g = lane >> 3;
+  const int src_lane = (lane >> 1) * 128 + 16 * (lane & 1);
+  const int dst_even = 8 * g + ((lane & 7) ^ g);
+  const int dst_odd = 8 * g + ((lane & 7) ^ g ^ 4);
+  auto issue = [&](int slab, int stage, int64_t head) {
+    if (head >= 0) {
+      const int8_t* src = p.codes + static_cast<uint64_t>(head) * kElements + kSlabKeys * slab + src_lane;
+      uint4* dst = ring + stage * kSlabChunks;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cp_async16(dst + 32 * i + ((i & 1) ? dst_odd : dst_even), src + 2048 * i);
+    }
+    cp_async_commit();  // one group per position, empty ones included
+  };
+
+  // Per-head inputs of the next item, fetched one head ahead.
+  float4 c_next = make_float4(0.F, 0.F, 0.F, 0.F), b_next = c_next;
+  uint2 q_next = make_uint2(0u, 0u);
+  auto fetch = [&](uint64_t item, int64_t head) {
+    if (head < 0) return;
+    c_next = __ldg(reinterpret_cast<const float4*>(p.smoothing + static_cast<uint64_t>(head) * kKeys) + lane);
+    b_next = __ldg(reinterpret_cast<const float4*>(p.scales + static_cast<uint64_t>(head) * kValues) + lane);
+    q_next = __ldg(reinterpret_cast<const uint2*>(p.queries + item * kKeys) + lane);
+  };
+  int64_t next_head = head_of(first);  // head of the item after the current one
+  fetch(first, next_head);
+  // Prologue: the first kSlabStages - 1 positions (slabs of the first item).
+#pragma unroll
+  for (int t = 0; t < kSlabStages - 1; ++t) issue(t, t, next_head);
+
+  const f2 magic = pack2(kCodeMagic, kCodeMagic);
+  const int swz = lane & 7;
+  int stage = 0;                              // ring stage of the current position
+  int ahead = kSlabStages - 1;                // ring stage of the position being issued
+  for (uint64_t item = first; item < p.items; item += stride) {
+    bool bad = false;
+    (void)resolve_item(p.map, item, &bad);
+    if (bad && lane == 0) report(p.status, kStatusBadSlot);
+    const int64_t head = next_head;
+    next_head = head_of(item + stride);
+    // (c_k, x_k) of this head into the warp's slots; the previous head's
+    // readers finished at the end of its last slab.
+    const float4 x4 = bf16x4_to_float4(q_next);
+    sh.cx[warp][2 * lane] = make_float4(c_next.x, x4.x, c_next.y, x4.y);
+    sh.cx[warp][2 * lane + 1] = make_float4(c_next.z, x4.z, c_next.w, x4.w);
+    if (kCompensated && head >= 0) {
+      const float4* kp = reinterpret_cast<const float4*>(p.compensator_keys) +
+                         static_cast<uint64_t>(head) * kKeys;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sh.kr[warp][4 * lane + i] = __ldg(kp + 4 * lane + i);
+    }
+    const float4 b4 = b_next;
+    fetch(item + stride, next_head);
+    f2 a01 = pack2(0.F, 0.F), a23 = a01, kp01 = a01, kp23 = a01;
+#pragma unroll 1
+    for (int s = 0; s < kSlabsPerHead; ++s) {
+      // Issue the position kSlabStages - 1 ahead: slab s + 2 of this item or
+      // slab s - 2 of the next one.
+      const int ahead_slab = s + kSlabStages - 1;
+      if (ahead_slab < kSlabsPerHead) {
+        issue(ahead_slab, ahead, head);
+      } else {
+        issue(ahead_slab - kSlabsPerHead, ahead, next_head);
+      }
+      ahead = ahead + 1 == kSlabStages ? 0 : ahead + 1;
+      cp_async_wait<kSlabStages - 1>();  // this position's slab has landed (own copies)
+      __syncwarp();                      // ... and every lane's copies are visible
+      if (head >= 0) {
+        const uint4* buf = ring + stage * kSlabChunks + lane * 8;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint4 r[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) r[j] = buf[(2 * j + half) ^ swz];
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t b0 = reinterpret_cast<const uint32_t*>(&r[0])[wi] ^ kCodeBias;
+            const uint32_t b1 = reinterpret_cast<const uint32_t*>(&r[1])[wi] ^ kCodeBias;
+            const uint32_t b2 = reinterpret_cast<const uint32_t*>(&r[2])[wi] ^ kCodeBias;
+            const uint32_t b3 = reinterpret_cast<const uint32_t*>(&r[3])[wi] ^ kCodeBias;
+            const int k0 = kSlabKeys * s + 16 * half + 4 * wi;
+#pragma unroll
+            for (int pair = 0; pair < 2; ++pair) {
+              const float4 cc = sh.cx[warp][(k0 >> 1) + pair];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int byte = 2 * pair + e;
+                const float c = e == 0 ? cc.x : cc.z, x = e == 0 ? cc.y : cc.w;
+                const f2 z01 = sub2(pack2(code_magic(b0, byte), code_magic(b1, byte)), magic);
+                const f2 z23 = sub2(pack2(code_magic(b2, byte), code_magic(b3, byte)), magic);
+                accumulate(a01, a23, z01, z23, c, x);
+                if (kCompensated) {
+                  const float4 kk = sh.kr[warp][k0 + byte];
+                  const f2 xx = pack2(x, x);
+                  kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
+                  kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
+                }
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();  // this slab (and after the last one, the head's slots) free again
+      stage = stage + 1 == kSlabStages ? 0 : stage + 1;
+    }
+    float* out = p.outputs + item * kValues + 4 * lane;
+    if (head < 0) {
+      *reinterpret_cast<float4*>(out) = make_float4(0.F, 0.F, 0.F, 0.F);
+    } else {
+      const float* vbase = kCompensated
+                               ? p.compensator_values +
+                                     (static_cast<uint64_t>(head) * kValues + 4 * lane) * kRank
+                               : nullptr;
+      __stcs(reinterpret_cast<float4*>(out),
+             finish_outputs(a01, a23, b4, kCompensated, kp01, kp23, vbase));
+    }
+  }
+  cp_async_wait<0>();  // no copy may still target this block's memory at exit
+}
+
+size_t project_smem_bytes(bool provider, bool compensated) {
+  if (provider) {
+    return compensated ? sizeof(ProviderProjectShared) : offsetof(ProviderProjectShared, kr);
+  }
+  return compensated ? sizeof(ProjectShared) : offsetof(ProjectShared, kr);
+}
+
+template <bool kProvider, bool kCompensated>
+constexpr auto project_kernel_for() {
+  if constexpr (kProvider) {
+    return project_provider_kernel<kCompensated>;
+  } else {
+    return project_kernel<kCompensated>;
+  }
 }
 
 template <bool kProvider, bool kCompensated>
@@ -252,15 +366,15 @@ cudaError_t launch_project_t(const ProjectParams& p, int grid, cudaStream_t stre
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kPThreads);
-  cfg.dynamicSmemBytes = project_smem_bytes(kProvider);
+  cfg.dynamicSmemBytes = project_smem_bytes(kProvider, kCompensated);
   cfg.stream = stream;
-  return cudaLaunchKernelEx(&cfg, project_kernel<kProvider, kCompensated>, p);
+  return cudaLaunchKernelEx(&cfg, project_kernel_for<kProvider, kCompensated>(), p);
 }
 
 template <bool kProvider, bool kCompensated>
 cudaError_t prepare_project_t(int* blocks_per_sm) {
-  auto kernel = project_kernel<kProvider, kCompensated>;
-  const size_t bytes = project_smem_bytes(kProvider);
+  auto kernel = project_kernel_for<kProvider, kCompensated>();
+  const size_t bytes = project_smem_bytes(kProvider, kCompensated);
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(bytes));
   if (err != cudaSuccess) return err;
