@@ -8,6 +8,7 @@
 
 #include "codec_device.cuh"
 #include "dequantize.cuh"
+#include "fit.cuh"
 #include "projection.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
@@ -41,6 +42,7 @@ struct DeviceSetup {
   int quantize_blocks[2][3] = {};  // [provider][mode] blocks per SM
   int dequantize_blocks[2][2] = {};
   int project_blocks[2][2] = {};
+  int fit_blocks = 0;
 };
 
 std::mutex g_setup_mutex;
@@ -79,6 +81,7 @@ const DeviceSetup* device_setup() {
       }
     }
   }
+  if (prepare_fit(&s.fit_blocks) != cudaSuccess || s.fit_blocks < 1) return nullptr;
   s.ready = true;
   return &s;
 }
@@ -131,6 +134,18 @@ int32_t run_project(void* stream, bool provider, const int8_t* codes, const floa
   return launch_project(provider, p, grid, static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? kOk
              : kLaunchFailed;
+}
+
+int32_t run_full(void* stream, bool provider, const float* dense, float* residual,
+                 float* smoothing, int8_t* codes, float* scales, float* ck, float* cv,
+                 uint64_t heads, uint32_t* status) {
+  const DeviceSetup* s = device_setup();
+  if (s == nullptr) return kSetupFailed;
+  FitParams f{dense, residual, ck, cv, heads, status, provider ? 1 : 0};
+  const int grid = grid_for(heads, s->sms, s->fit_blocks);
+  if (launch_fit(f, grid, static_cast<cudaStream_t>(stream)) != cudaSuccess) return kLaunchFailed;
+  return run_quantize(stream, provider, kFused, residual, nullptr, smoothing, codes, scales, heads,
+                      SlotMap{nullptr, 1, 1}, status);
 }
 
 bool compensators_ok(const float* ck, const float* cv) {
@@ -357,6 +372,23 @@ int32_t statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1(
   return gdnsc::run_project(stream, layout == 1u, codes_cache, smoothing_cache, scales_cache,
                             compensator_keys_cache, compensator_values_cache, queries_bf16,
                             outputs, items, SlotMap{slot_ids, heads_per_slot, num_slots}, status);
+}
+
+// ---- Full codec ------------------------------------------------------------------
+
+int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
+    void* stream, uint32_t layout, const float* dense, float* residual_workspace,
+    float* smoothing, int8_t* quantized, float* value_scales, float* compensator_keys,
+    float* compensator_values, uint32_t states, uint32_t* status) {
+  if (layout > 1u || dense == nullptr || residual_workspace == nullptr || smoothing == nullptr ||
+      quantized == nullptr || value_scales == nullptr || compensator_keys == nullptr ||
+      compensator_values == nullptr || states == 0u || !aligned16(dense) ||
+      !aligned16(residual_workspace) || !aligned16(smoothing) || !aligned16(quantized) ||
+      !aligned16(value_scales) || !aligned16(compensator_keys) || !aligned16(compensator_values)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_full(stream, layout == 1u, dense, residual_workspace, smoothing, quantized,
+                         value_scales, compensator_keys, compensator_values, states, status);
 }
 
 // ---- Status and synthetic inputs --------------------------------------------------

@@ -44,6 +44,9 @@ SIGNATURES: dict[str, list] = {
         [_vp, _u32] + [_vp] * 7 + [_u32, _u32, _u32, _vp],
     "statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1":
         [_vp, _u32] + [_vp] * 8 + [_u32, _u32, _u32, _vp],
+    # full codec (rank-4 fit + int8 stage)
+    "statecentric_gdn_state_codec_full_initialize_launch_v1":
+        [_vp, _u32] + [_vp] * 7 + [_u32, _vp],
     # status and benchmark support
     "statecentric_gdn_state_codec_device_error_v1": [_vp, _i32],
     "statecentric_gdn_state_codec_synthesize_states_v1":

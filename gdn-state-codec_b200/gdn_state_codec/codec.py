@@ -252,6 +252,42 @@ def encoded_projection(encoded: EncodedStates, queries: torch.Tensor, *,
     return out
 
 
+@dataclass
+class FullEncoded:
+    """The reference's full boundary of each head: int8 codes, smoothing and
+    scales of the residual, the rank-4 compensators K [.., 128 keys, 4] and
+    V [.., 128 values, 4], and the fp32 residual the codes encode."""
+
+    encoded: EncodedStates
+    compensator_keys: torch.Tensor
+    compensator_values: torch.Tensor
+    residual: torch.Tensor
+
+
+def full_encode(states: torch.Tensor, layout: str = "capsule", *,
+                status: torch.Tensor | None = None) -> FullEncoded:
+    """FromDenseBoundary's encode (capsule.cpp:129-225) of every head: the
+    rank-4 compensator fit, then smoothing + int8 quantize of the residual,
+    bit-identical to the portable C++ codec.  Non-finite data sets bit 2 of
+    ``status`` (int32 device scalar, optional) and of the device error word."""
+    heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    _heads_ok(heads)
+    code = _layout(layout)
+    device = states.device
+    lead = tuple(states.shape[:-2])
+    out = empty_encoded(lead, layout, device)
+    keys = torch.empty((*lead, KEY_DIMENSION, COMPENSATOR_RANK), dtype=torch.float32, device=device)
+    values = torch.empty((*lead, VALUE_DIMENSION, COMPENSATOR_RANK), dtype=torch.float32,
+                         device=device)
+    residual = torch.empty_like(states)
+    with torch.cuda.device(device):
+        _status("full encode", _native.call(
+            "statecentric_gdn_state_codec_full_initialize_launch_v1", _stream(device), code,
+            _ptr(states), _ptr(residual), _ptr(out.smoothing), _ptr(out.codes), _ptr(out.scales),
+            _ptr(keys), _ptr(values), heads, _ptr(status)))
+    return FullEncoded(out, keys, values, residual)
+
+
 # ---------------------------------------------------------------------------
 # Slot-indexed caches ([num_slots, heads_per_slot, ...], slot-major).
 
@@ -345,7 +381,8 @@ def encoded_projection_indexed(encoded_cache: EncodedStates, queries: torch.Tens
 # Status and synthetic inputs.
 
 def device_error(device: torch.device | str | int = "cuda", clear: bool = False) -> int:
-    """Sticky error bits of the device: 1 = invalid slot id, 2 = wait timeout."""
+    """Sticky error bits of the device: 1 = invalid slot id, 2 = wait timeout,
+    4 = non-finite data in a full-codec fit."""
     bits = ctypes.c_uint32(0)
     with torch.cuda.device(device):
         _status("device error query", _native.call(

@@ -166,11 +166,32 @@ int32_t statecentric_gdn_state_codec_encoded_projection_indexed_launch_v1(
     uint32_t count, uint32_t heads_per_slot, uint32_t num_slots,
     uint32_t* status);
 
+/* ---- Full codec ------------------------------------------------------------ */
+
+/* The reference's full encode (FromDenseBoundary's QuantizeBoundary,
+ * capsule.cpp:129-225) of `states` heads: the rank-4 compensator fit (32 power
+ * iterations per rank, deflation) bit-identical to the portable C++ codec,
+ * then smoothing + int8 quantize of the residual.  `layout` 0: dense is
+ * capsule [state][key][value]; 1: provider [state][value][key] (the fit runs
+ * on the [key][value] matrix either way).  Outputs: residual_workspace (the
+ * fp32 residual the int8 stage encodes, in the input's layout), smoothing
+ * [state][128], quantized codes (input's layout), value_scales [state][128],
+ * compensator_keys [state][128 keys][4] and compensator_values [state][128
+ * values][4] fp32 -- the planes of the reference's serialized boundary.
+ * Heads with non-finite input or singular value (which the reference rejects)
+ * set bit 2 (value 4) of *status (optional) and of the sticky error word;
+ * their outputs are unspecified. */
+int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
+    void* stream, uint32_t layout, const float* dense, float* residual_workspace,
+    float* smoothing, int8_t* quantized, float* value_scales, float* compensator_keys,
+    float* compensator_values, uint32_t states, uint32_t* status);
+
 /* ---- Library status and benchmark support ------------------------------- */
 
 /* Read (and with clear != 0 reset) the sticky per-device error word of the
  * current device: bit 0 = an invalid slot id was seen, bit 1 = a bounded
- * device wait expired.  Synchronous. */
+ * device wait expired, bit 2 = non-finite data in a full-codec fit.
+ * Synchronous. */
 int32_t statecentric_gdn_state_codec_device_error_v1(uint32_t* bits, int32_t clear);
 
 /* Seeded synthetic inputs (benchmark and test support): `slots` slots of

@@ -59,6 +59,16 @@ def declared_symbols() -> set[str]:
     return names
 
 
+def declared_arity() -> dict[str, int]:
+    """Parameter count of every declared entry point."""
+    arity: dict[str, int] = {}
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        for name, params in re.findall(rf"\b({PREFIX}\w+)\s*\(([^)]*)\)\s*;", text):
+            arity[name] = len([p for p in params.split(",") if p.strip()])
+    return arity
+
+
 def lib():
     return _native.load()
 
@@ -80,6 +90,10 @@ def test_every_declared_entry_point_is_exported_and_bound():
         f"{sorted(names ^ set(_native.SIGNATURES))}")
     for name in names:
         assert hasattr(lib(), name), name
+    arity = declared_arity()
+    assert set(arity) == names
+    for name, argtypes in _native.SIGNATURES.items():
+        assert len(argtypes) == arity[name], (name, len(argtypes), arity[name])
 
 
 @pytest.mark.parametrize("library", sorted(REFERENCE_LIBRARIES))
@@ -145,6 +159,14 @@ def test_indexed_geometry_is_validated():
     assert call("dequantize_indexed_launch_v1", n, 1, a, a, a, a, n, a, a, 4, 32, 8, n) == BAD_ARGS
     assert call("encoded_projection_indexed_launch_v1",
                 n, 0, a, a, a, n, n, a, a, a, 4, 32, 0, n) == BAD_ARGS
+
+
+def test_full_codec_entry_point_validates():
+    a, n = ALIGNED, None
+    assert call("full_initialize_launch_v1", n, 2, a, a, a, a, a, a, a, 1, n) == BAD_ARGS
+    assert call("full_initialize_launch_v1", n, 0, a, a, a, a, a, a, a, 0, n) == BAD_ARGS
+    assert call("full_initialize_launch_v1", n, 0, a, n, a, a, a, a, a, 1, n) == BAD_ARGS
+    assert call("full_initialize_launch_v1", n, 1, a, a, a, a, a, a, MISALIGNED, 1, n) == BAD_ARGS
 
 
 def test_status_and_support_entry_points_validate():
