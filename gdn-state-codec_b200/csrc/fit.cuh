@@ -92,7 +92,7 @@ __device__ __forceinline__ bool fit_normalize(FitShared& sh, float* vec, float& 
 }
 
 __global__ void __launch_bounds__(kFitThreads) fit_kernel(FitParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   FitShared& sh = *reinterpret_cast<FitShared*>(smem_raw);
   const int t = threadIdx.x;
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
