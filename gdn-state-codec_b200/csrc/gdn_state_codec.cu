@@ -391,6 +391,63 @@ int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
                          value_scales, compensator_keys, compensator_values, states, status);
 }
 
+// ---- Full codec without a caller workspace ----------------------------------------
+//
+// Some callers cannot allocate device memory on the call path: a serving
+// engine that has already handed nearly all of the GPU's memory to its state
+// and KV cache pools after profiling, or a host process that owns every
+// device allocation; cudaMalloc would also synchronize the device.  For them
+// the full encode can keep the residual between its two stages in a static
+// device array instead of a caller workspace.  The array is loaded with the
+// library and held by every GPU that loads it until the process exits.
+
+namespace gdnsc {
+namespace {
+
+constexpr uint32_t kStaticFullMaxStates = 64;  // 64 heads x 64 KiB = 4 MiB
+static __device__ __align__(256) float g_full_residual_scratch[kStaticFullMaxStates * kElements];
+
+std::mutex g_scratch_mutex;
+float* g_scratch_address[kMaxDevices] = {};
+
+// Device address of the static array on the current device, looked up once
+// per device (the array's host-side name is not a device address).
+float* static_full_scratch() {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_address[device] == nullptr) {
+    void* address = nullptr;
+    if (cudaGetSymbolAddress(&address, g_full_residual_scratch) != cudaSuccess) return nullptr;
+    g_scratch_address[device] = static_cast<float*>(address);
+  }
+  return g_scratch_address[device];
+}
+
+}  // namespace
+}  // namespace gdnsc
+
+int32_t statecentric_gdn_state_codec_full_initialize_static_launch_v1(
+    void* stream, uint32_t layout, const float* dense, float* smoothing, int8_t* quantized,
+    float* value_scales, float* compensator_keys, float* compensator_values, uint32_t states,
+    uint32_t* status) {
+  if (states > gdnsc::kStaticFullMaxStates) return gdnsc::kBadArgs;  // over the array's size
+  if (layout > 1u || dense == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || compensator_keys == nullptr || compensator_values == nullptr ||
+      states == 0u || !aligned16(dense) || !aligned16(smoothing) || !aligned16(quantized) ||
+      !aligned16(value_scales) || !aligned16(compensator_keys) || !aligned16(compensator_values)) {
+    return gdnsc::kBadArgs;
+  }
+  float* scratch = gdnsc::static_full_scratch();
+  if (scratch == nullptr) return gdnsc::kSetupFailed;
+  // The fit overwrites every element of the scratch it uses before the int8
+  // stage reads it, so nothing left by an earlier call needs clearing.
+  return gdnsc::run_full(stream, layout == 1u, dense, scratch, smoothing, quantized,
+                         value_scales, compensator_keys, compensator_values, states, status);
+}
+
 // ---- Status and synthetic inputs --------------------------------------------------
 
 int32_t statecentric_gdn_state_codec_device_error_v1(uint32_t* bits, int32_t clear) {

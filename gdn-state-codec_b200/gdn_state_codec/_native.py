@@ -47,6 +47,8 @@ SIGNATURES: dict[str, list] = {
     # full codec (rank-4 fit + int8 stage)
     "statecentric_gdn_state_codec_full_initialize_launch_v1":
         [_vp, _u32] + [_vp] * 7 + [_u32, _vp],
+    "statecentric_gdn_state_codec_full_initialize_static_launch_v1":
+        [_vp, _u32] + [_vp] * 6 + [_u32, _vp],
     # status and benchmark support
     "statecentric_gdn_state_codec_device_error_v1": [_vp, _i32],
     "statecentric_gdn_state_codec_synthesize_states_v1":

@@ -186,6 +186,23 @@ int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
     float* smoothing, int8_t* quantized, float* value_scales, float* compensator_keys,
     float* compensator_values, uint32_t states, uint32_t* status);
 
+/* full_initialize_launch_v1 without a residual workspace, for callers that
+ * cannot allocate device memory on the call path (a serving engine whose
+ * memory is already handed to its cache pools, a host that owns every device
+ * allocation; cudaMalloc would also synchronize the device).  No counterpart
+ * in the reference.  The residual between the fit and the int8 stage lives in
+ * a static device array of 64 heads (4 MiB) that every GPU loading the
+ * library holds until exit; `states` above 64 is rejected with 1.  The first
+ * call on a device looks up the array's device address (make it before any
+ * stream capture on that device).  All calls on a device share its array,
+ * which keeps the last call's contents: calls that can overlap on that GPU
+ * (for example on different streams) race and must be serialized by the
+ * caller.  Allocates nothing. */
+int32_t statecentric_gdn_state_codec_full_initialize_static_launch_v1(
+    void* stream, uint32_t layout, const float* dense, float* smoothing, int8_t* quantized,
+    float* value_scales, float* compensator_keys, float* compensator_values, uint32_t states,
+    uint32_t* status);
+
 /* ---- Library status and benchmark support ------------------------------- */
 
 /* Read (and with clear != 0 reset) the sticky per-device error word of the
