@@ -332,6 +332,9 @@ def main() -> None:
     barrier()
     proj_ms = max_over_ranks(p_start.elapsed_time(p_end)) / proj_iters
 
+    # ---- full codec (rank-4 fit + int8 stage) on a smaller batch --------------
+    full = full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank)
+
     # ---- end to end through the public API with host buffers -----------------
     e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
                       max_over_ranks, world)
@@ -373,6 +376,7 @@ def main() -> None:
                 "bytes_per_head": BYTES_PER_HEAD[dominant], "heads_per_launch": heads,
             },
             "e2e": e2e,
+            "full_codec": full,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
@@ -381,6 +385,59 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank):
+    """The reference's full encode (FromDenseBoundary: rank-4 fit + int8 stage)
+    on 8 slots x 30 layers x 32 heads per GPU, against the reference library
+    itself on the host cores (bounded sample) on rank 0."""
+    slots = 8
+    heads = slots * LAYERS * HEADS
+    states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=2,
+                                     slot_base=rank * slots, device=device)
+    for _ in range(2):
+        codec.full_encode(states, layout)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    iters = 3
+    start.record(stream)
+    for _ in range(iters):
+        codec.full_encode(states, layout)
+    end.record(stream)
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end)) / iters
+    result = {"heads": heads, "ms": ms, "states_per_s": heads / (ms / 1e3),
+              "bit_exact_to": "FromDenseBoundary (tests/test_gpu_full.py)"}
+    if rank == 0:
+        result["cpu_reference"] = full_codec_cpu_reference()
+    return result
+
+
+def full_codec_cpu_reference(sample_heads: int = 512, target_seconds: float = 2.0):
+    """FromDenseBoundary of the reference library (oracle/_ref, compiled from
+    native/src) on all host cores, repeated over a bounded sample of heads
+    for about ``target_seconds``."""
+    import concurrent.futures
+
+    import oracle as oracle_mod  # noqa: PLC0415 - baseline only
+
+    if not oracle_mod.ref_available():
+        return None
+    cores = os.cpu_count() or 1
+    states = sample_states("capsule", sample_heads)
+    oracle_mod.ref_codec_head(states[0])  # warm-up
+    done, t0 = 0, time.perf_counter()
+    with concurrent.futures.ThreadPoolExecutor(max_workers=cores) as pool:
+        while True:
+            list(pool.map(oracle_mod.ref_codec_head, states))
+            done += sample_heads
+            elapsed = time.perf_counter() - t0
+            if elapsed >= target_seconds:
+                break
+    return {"states_per_s": done / elapsed, "cores": cores, "kind": "reference",
+            "sample": f"{done} heads ({sample_heads} distinct), FromDenseBoundary of "
+                      f"oracle/_ref/libgdn_ref.so on {cores} threads, {elapsed:.2f} s wall"}
 
 
 def committed_traffic(kernel: str, heads: int):
