@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "capsule.cuh"
 #include "codec_device.cuh"
 #include "dequantize.cuh"
 #include "fit.cuh"
@@ -82,6 +83,7 @@ const DeviceSetup* device_setup() {
     }
   }
   if (prepare_fit(&s.fit_blocks) != cudaSuccess || s.fit_blocks < 1) return nullptr;
+  if (prepare_capsule() != cudaSuccess) return nullptr;
   s.ready = true;
   return &s;
 }
@@ -389,6 +391,85 @@ int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
   }
   return gdnsc::run_full(stream, layout == 1u, dense, residual_workspace, smoothing, quantized,
                          value_scales, compensator_keys, compensator_values, states, status);
+}
+
+// ---- Capsule wire format ------------------------------------------------------------
+
+namespace gdnsc {
+namespace {
+
+bool identity_ok(const char* geometry, uint64_t generation, uint64_t epoch) {
+  return geometry != nullptr && lowercase_hex64(geometry) && generation > 0 && epoch > 0;
+}
+
+CapsuleIdentity make_identity(const char* geometry, uint64_t generation, uint64_t epoch) {
+  CapsuleIdentity id{};
+  std::memcpy(id.geometry, geometry, sizeof(id.geometry));
+  id.generation = generation;
+  id.epoch = epoch;
+  return id;
+}
+
+}  // namespace
+}  // namespace gdnsc
+
+int32_t statecentric_gdn_state_codec_capsule_serialize_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes, const float* smoothing,
+    const float* scales, const float* compensator_keys, const float* compensator_values,
+    const char* model_geometry_sha256, uint64_t generation, uint64_t epoch, uint8_t* capsules,
+    uint32_t states) {
+  if (layout > 1u || codes == nullptr || smoothing == nullptr || scales == nullptr ||
+      capsules == nullptr || states == 0u || !aligned16(codes) || !aligned16(smoothing) ||
+      !aligned16(scales) || !aligned8(capsules) ||
+      !gdnsc::compensators_ok(compensator_keys, compensator_values) ||
+      !gdnsc::identity_ok(model_geometry_sha256, generation, epoch)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::SerializeParams p{codes, smoothing, scales, compensator_keys, compensator_values,
+                           capsules, states, static_cast<int>(layout),
+                           gdnsc::make_identity(model_geometry_sha256, generation, epoch)};
+  const auto st = static_cast<cudaStream_t>(stream);
+  constexpr int kWarps = gdnsc::kCapsuleThreads / 32;
+  const int assemble_grid = gdnsc::grid_for((states + kWarps - 1) / kWarps, s->sms, 16);
+  gdnsc::capsule_assemble_kernel<<<assemble_grid, gdnsc::kCapsuleThreads, 0, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return gdnsc::kLaunchFailed;
+  const unsigned digest_grid = (states + gdnsc::kCapsuleThreads - 1) / gdnsc::kCapsuleThreads;
+  gdnsc::capsule_digest_kernel<<<digest_grid, gdnsc::kCapsuleThreads, 0, st>>>(capsules, states);
+  return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
+}
+
+int32_t statecentric_gdn_state_codec_capsule_restore_launch_v1(
+    void* stream, uint32_t layout, const uint8_t* capsules, const char* model_geometry_sha256,
+    uint64_t generation, uint64_t epoch, int8_t* codes, float* smoothing, float* scales,
+    float* compensator_keys, float* compensator_values, int32_t* head_status, uint32_t states) {
+  if (layout > 1u || capsules == nullptr || codes == nullptr || smoothing == nullptr ||
+      scales == nullptr || compensator_keys == nullptr || compensator_values == nullptr ||
+      head_status == nullptr || states == 0u || !aligned8(capsules) || !aligned16(codes) ||
+      !aligned16(smoothing) || !aligned16(scales) || !aligned16(compensator_keys) ||
+      !aligned16(compensator_values) || (reinterpret_cast<uintptr_t>(head_status) & 3u) != 0 ||
+      !gdnsc::identity_ok(model_geometry_sha256, generation, epoch)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::RestoreParams p{capsules, codes, smoothing, scales, compensator_keys,
+                         compensator_values, head_status, states, static_cast<int>(layout),
+                         gdnsc::make_identity(model_geometry_sha256, generation, epoch)};
+  const unsigned grid = (states + gdnsc::kCapsuleThreads - 1) / gdnsc::kCapsuleThreads;
+  gdnsc::capsule_restore_kernel<<<grid, gdnsc::kCapsuleThreads, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
+}
+
+int32_t statecentric_gdn_state_codec_sha256_v1(const uint8_t* data, uint64_t size,
+                                               char* hex64) {
+  if ((data == nullptr && size != 0) || hex64 == nullptr) return gdnsc::kBadArgs;
+  uint32_t h[8];
+  gdnsc::sha256(data, size, h);
+  gdnsc::sha256_hex(h, hex64);
+  return gdnsc::kOk;
 }
 
 // ---- Full codec without a caller workspace ----------------------------------------

@@ -49,6 +49,12 @@ SIGNATURES: dict[str, list] = {
         [_vp, _u32] + [_vp] * 7 + [_u32, _vp],
     "statecentric_gdn_state_codec_full_initialize_static_launch_v1":
         [_vp, _u32] + [_vp] * 6 + [_u32, _vp],
+    # capsule wire format
+    "statecentric_gdn_state_codec_capsule_serialize_launch_v1":
+        [_vp, _u32] + [_vp] * 6 + [_u64, _u64, _vp, _u32],
+    "statecentric_gdn_state_codec_capsule_restore_launch_v1":
+        [_vp, _u32, _vp, _vp, _u64, _u64] + [_vp] * 6 + [_u32],
+    "statecentric_gdn_state_codec_sha256_v1": [_vp, _u64, _vp],
     # status and benchmark support
     "statecentric_gdn_state_codec_device_error_v1": [_vp, _i32],
     "statecentric_gdn_state_codec_synthesize_states_v1":

@@ -289,6 +289,85 @@ def full_encode(states: torch.Tensor, layout: str = "capsule", *,
 
 
 # ---------------------------------------------------------------------------
+# The reference's capsule wire format (Serialize / Restore).
+
+CAPSULE_BYTES = 21688
+CAPSULE_STATUS = {
+    0: "restored", 1: "capsule magic differs", 2: "checksum encoding is invalid",
+    3: "checksum differs", 4: "quantization parameters differ",
+    5: "identity or geometry differs", 6: "window position differs",
+    7: "INT8 residual contains -128", 8: "boundary payload is invalid",
+    9: "restored state is non-finite",
+}
+
+
+def _identity(geometry: str, generation: int, epoch: int):
+    raw = geometry.encode("ascii")
+    if len(raw) != 64 or any(c not in b"0123456789abcdef" for c in raw):
+        raise ValueError("model geometry digest must be 64 lowercase hex characters")
+    if generation <= 0 or epoch <= 0:
+        raise ValueError("generation and epoch must be positive")
+    return ctypes.c_char_p(raw), generation, epoch
+
+
+def serialize_capsules(encoded: EncodedStates, *, geometry: str, generation: int, epoch: int,
+                       compensator_keys: torch.Tensor | None = None,
+                       compensator_values: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's Serialize of every encoded head: uint8 [heads, 21688],
+    byte-identical to GdnStateCodecCapsule::Serialize (capsule.cpp:446-475)."""
+    heads = _check_encoded(encoded)
+    _heads_ok(heads)
+    device = encoded.codes.device
+    ck, cv = _compensators(heads, device, compensator_keys, compensator_values)
+    geo, generation, epoch = _identity(geometry, generation, epoch)
+    if out is None:
+        out = torch.empty((heads, CAPSULE_BYTES), dtype=torch.uint8, device=device)
+    if _check(out, "capsules", torch.uint8, (CAPSULE_BYTES,), device) != heads:
+        raise ValueError("capsule buffer must hold one capsule per head")
+    with torch.cuda.device(device):
+        _status("capsule serialize", _native.call(
+            "statecentric_gdn_state_codec_capsule_serialize_launch_v1", _stream(device),
+            LAYOUTS[encoded.layout], _ptr(encoded.codes), _ptr(encoded.smoothing),
+            _ptr(encoded.scales), _ptr(ck), _ptr(cv), geo, generation, epoch, _ptr(out), heads))
+    return out
+
+
+def restore_capsules(capsules: torch.Tensor, layout: str = "capsule", *, geometry: str,
+                     generation: int, epoch: int):
+    """The reference's Restore of each capsule, fail-closed per head: returns
+    (EncodedStates, compensator_keys, compensator_values, status int32 [heads]);
+    status 0 = restored, else the first failing check (CAPSULE_STATUS)."""
+    heads = _check(capsules, "capsules", torch.uint8, (CAPSULE_BYTES,))
+    _heads_ok(heads)
+    device = capsules.device
+    code = _layout(layout)
+    geo, generation, epoch = _identity(geometry, generation, epoch)
+    lead = tuple(capsules.shape[:-1])
+    encoded = empty_encoded(lead, layout, device)
+    keys = torch.zeros((*lead, KEY_DIMENSION, COMPENSATOR_RANK), dtype=torch.float32, device=device)
+    values = torch.zeros((*lead, VALUE_DIMENSION, COMPENSATOR_RANK), dtype=torch.float32,
+                         device=device)
+    status = torch.empty(lead, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        _status("capsule restore", _native.call(
+            "statecentric_gdn_state_codec_capsule_restore_launch_v1", _stream(device), code,
+            _ptr(capsules), geo, generation, epoch, _ptr(encoded.codes), _ptr(encoded.smoothing),
+            _ptr(encoded.scales), _ptr(keys), _ptr(values), _ptr(status), heads))
+    return encoded, keys, values, status
+
+
+def sha256_hex(data: bytes) -> str:
+    """SHA-256 of host bytes by the library's own implementation (test support)."""
+    buffer = ctypes.create_string_buffer(bytes(data), len(data)) if data else None
+    out = ctypes.create_string_buffer(64)
+    _status("sha256", _native.call("statecentric_gdn_state_codec_sha256_v1",
+                                   ctypes.cast(buffer, ctypes.c_void_p) if buffer else None,
+                                   len(data), out))
+    return out.raw.decode("ascii")
+
+
+# ---------------------------------------------------------------------------
 # Slot-indexed caches ([num_slots, heads_per_slot, ...], slot-major).
 
 def _slot_geometry(cache_heads: int, cache: torch.Tensor, slot_ids: torch.Tensor,

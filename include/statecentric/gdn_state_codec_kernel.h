@@ -186,6 +186,44 @@ int32_t statecentric_gdn_state_codec_full_initialize_launch_v1(
     float* smoothing, int8_t* quantized, float* value_scales, float* compensator_keys,
     float* compensator_values, uint32_t states, uint32_t* status);
 
+/* ---- Capsule wire format ---------------------------------------------------- */
+
+/* Bytes of one serialized boundary capsule: 128 x 128 head, rank-4
+ * compensators, window position 0 (120-byte header + 21,504-byte payload +
+ * 64-character digest). */
+#define STATECENTRIC_GDN_STATE_CODEC_CAPSULE_BYTES 21688u
+
+/* The reference's Serialize (capsule.cpp:446-475) of `states` encoded heads,
+ * byte for byte: capsule h is written at capsules + h * 21688 (8-byte
+ * aligned).  Codes in `layout` 0 (capsule [key][value]) or 1 (provider
+ * [value][key]); compensators [state][128][4] fp32, or both NULL for the
+ * quant-only format (serialized as zeros).  The identity (64 lowercase hex
+ * characters, HOST pointer; generation > 0; epoch > 0) is the same for every
+ * capsule.  Runs on the stream; the SHA-256 digests are computed on the
+ * device. */
+int32_t statecentric_gdn_state_codec_capsule_serialize_launch_v1(
+    void* stream, uint32_t layout, const int8_t* codes, const float* smoothing,
+    const float* scales, const float* compensator_keys, const float* compensator_values,
+    const char* model_geometry_sha256, uint64_t generation, uint64_t epoch,
+    uint8_t* capsules, uint32_t states);
+
+/* The reference's Restore (capsule.cpp:477-578) of `states` capsules under
+ * the expected identity, default parameters and window position 0, fail-closed
+ * per head: head_status[h] (device int32) = 0 when restored, else the first
+ * failing check in the reference's order -- 1 magic, 2 checksum encoding,
+ * 3 checksum, 4 parameters, 5 identity or geometry, 6 window position,
+ * 7 a -128 code, 8 invalid boundary payload, 9 non-finite dense state.
+ * Nothing is written for a rejected head. */
+int32_t statecentric_gdn_state_codec_capsule_restore_launch_v1(
+    void* stream, uint32_t layout, const uint8_t* capsules, const char* model_geometry_sha256,
+    uint64_t generation, uint64_t epoch, int8_t* codes, float* smoothing, float* scales,
+    float* compensator_keys, float* compensator_values, int32_t* head_status, uint32_t states);
+
+/* Test support: SHA-256 (FIPS 180-4) of `size` HOST bytes as 64 lowercase hex
+ * characters (not terminated), computed on the host by the same code the
+ * capsule kernels run.  Synchronous. */
+int32_t statecentric_gdn_state_codec_sha256_v1(const uint8_t* data, uint64_t size, char* hex64);
+
 /* full_initialize_launch_v1 without a residual workspace, for callers that
  * cannot allocate device memory on the call path (a serving engine whose
  * memory is already handed to its cache pools, a host that owns every device

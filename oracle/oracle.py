@@ -340,3 +340,49 @@ def ref_quant_project(codes, c, b, queries, threads: int = 1) -> np.ndarray:
     if status != 0:
         raise ValueError("reference readout rejected the input")
     return out
+
+
+# --------------------------------------------------------------------------
+# The reference's capsule wire format (Serialize / Restore, capsule.cpp:446-578).
+
+DEFAULT_GEOMETRY = "a" * 64   # the identity the shim's codec helpers use
+CAPSULE_BYTES = 21688          # 128 x 128 head, rank 4, no buffered updates
+
+
+def _ref_capsule_api() -> ctypes.CDLL:
+    handle = ref()
+    if not getattr(handle, "_capsule_bound", False):
+        u32, u64 = ctypes.c_uint32, ctypes.c_uint64
+        handle.ref_serialize_head.argtypes = [_f32p, u32, u32, ctypes.c_char_p, u64, u64,
+                                              ctypes.c_void_p, u64]
+        handle.ref_serialize_head.restype = u64
+        handle.ref_restore_capsule.argtypes = [ctypes.c_void_p, u64, ctypes.c_char_p, u64, u64,
+                                               u32, u32, ctypes.c_char_p, u64]
+        handle.ref_restore_capsule.restype = ctypes.c_int
+        handle._capsule_bound = True
+    return handle
+
+
+def ref_serialize_head(dense: np.ndarray, geometry: str = DEFAULT_GEOMETRY,
+                       generation: int = 7, epoch: int = 11) -> bytes:
+    """Serialize(FromDenseBoundary(dense)) of the reference library."""
+    dense = np.ascontiguousarray(dense, dtype=np.float32)
+    keys, values = dense.shape
+    out = np.empty(1 << 20, np.uint8)
+    size = _ref_capsule_api().ref_serialize_head(
+        _ptr(dense, _f32p), keys, values, geometry.encode(), generation, epoch,
+        out.ctypes.data, out.size)
+    if size == 0:
+        raise ValueError("reference rejected the input")
+    return out[:size].tobytes()
+
+
+def ref_restore_capsule(data: bytes, geometry: str = DEFAULT_GEOMETRY, generation: int = 7,
+                        epoch: int = 11, keys: int = 128, values: int = 128) -> tuple[bool, str]:
+    """Restore() of the reference library: (accepted, rejection message)."""
+    buffer = np.frombuffer(data, np.uint8).copy()
+    message = ctypes.create_string_buffer(256)
+    status = _ref_capsule_api().ref_restore_capsule(
+        buffer.ctypes.data, buffer.size, geometry.encode(), generation, epoch, keys, values,
+        message, 256)
+    return status == 0, message.value.decode()

@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <span>
 #include <string>
 #include <vector>
 
@@ -141,6 +142,59 @@ extern "C" int ref_head_bytes(std::uint32_t keys, std::uint32_t values,
     *boundary_bytes = capsule.compressed_boundary_bytes();
     return 0;
   } catch (const std::exception&) {
+    return 1;
+  }
+}
+
+namespace {
+
+GdnStateCodecIdentity IdentityOf(const char* geometry64, std::uint64_t generation,
+                                 std::uint64_t epoch, std::uint32_t keys, std::uint32_t values) {
+  return {std::string(geometry64, 64), generation, epoch, keys, values};
+}
+
+}  // namespace
+
+// The reference's serialized capsule (Serialize, capsule.cpp:446-475) of
+// FromDenseBoundary(dense) under the given identity, written to `out`.
+// Returns the byte count, or 0 when the reference rejects the input or the
+// buffer is too small.
+extern "C" std::uint64_t ref_serialize_head(const float* dense, std::uint32_t keys,
+                                            std::uint32_t values, const char* geometry64,
+                                            std::uint64_t generation, std::uint64_t epoch,
+                                            std::uint8_t* out, std::uint64_t capacity) {
+  try {
+    const std::size_t elements = static_cast<std::size_t>(keys) * values;
+    std::vector<float> state(dense, dense + elements);
+    const auto capsule = GdnStateCodecCapsule::FromDenseBoundary(
+        state, IdentityOf(geometry64, generation, epoch, keys, values), GdnStateCodecParameters{});
+    const auto bytes = capsule.Serialize();
+    if (bytes.size() > capacity) return 0;
+    std::memcpy(out, bytes.data(), bytes.size());
+    return bytes.size();
+  } catch (const std::exception&) {
+    return 0;
+  }
+}
+
+// The reference's Restore (capsule.cpp:477-578) of `bytes` with the expected
+// identity, default parameters and window position 0.  Returns 0 when it
+// accepts, 1 when it rejects; the rejection message goes to `message`.
+extern "C" int ref_restore_capsule(const std::uint8_t* bytes, std::uint64_t size,
+                                   const char* geometry64, std::uint64_t generation,
+                                   std::uint64_t epoch, std::uint32_t keys, std::uint32_t values,
+                                   char* message, std::uint64_t message_capacity) {
+  try {
+    (void)GdnStateCodecCapsule::Restore(
+        std::span<const std::uint8_t>(bytes, size),
+        IdentityOf(geometry64, generation, epoch, keys, values), GdnStateCodecParameters{}, 0);
+    if (message && message_capacity) message[0] = '\0';
+    return 0;
+  } catch (const std::exception& error) {
+    if (message && message_capacity) {
+      std::strncpy(message, error.what(), message_capacity - 1);
+      message[message_capacity - 1] = '\0';
+    }
     return 1;
   }
 }
