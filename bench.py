@@ -56,6 +56,9 @@ def parse_args():
                         help="request slots per GPU (default: config 2's 64)")
     parser.add_argument("--profile", action="store_true",
                         help="device-resident steps only (for ncu captures of a small case)")
+    parser.add_argument("--profile-full", action="store_true",
+                        help="device-resident full-codec launches only (fit + quantize), "
+                             "warm-up + steps of them, for ncu captures of the fit kernel")
     return parser.parse_args()
 
 
@@ -230,7 +233,7 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.warmup < 3 and not args.profile:
+    if args.warmup < 3 and not (args.profile or args.profile_full):
         raise SystemExit("--warmup must be >= 3")
 
     import torch
@@ -264,6 +267,16 @@ def main() -> None:
     layout = args.layout
     states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=0,
                                      slot_base=shard.base, device=device)
+    if args.profile_full:
+        for _ in range(args.warmup + args.steps):
+            codec.full_encode(states, layout)
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile_full": True, "heads": heads,
+                              "launches": args.warmup + args.steps}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     encoded = codec.empty_encoded((slots, LAYERS, HEADS), layout, device)
     dense = torch.empty_like(states)
     stream = torch.cuda.current_stream(device)
@@ -339,6 +352,15 @@ def main() -> None:
     e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
                       max_over_ranks, world)
 
+    # ---- configs 4 and 5 on their own caches (the config-2 buffers freed) ----
+    del states, dense, encoded, queries, outputs
+    torch.cuda.empty_cache()
+    ragged = ragged_measure(codec, torch, layout, device, barrier, rank, world)
+    torch.cuda.empty_cache()
+    box = box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
+                      rank, world)
+    torch.cuda.empty_cache()
+
     if rank == 0:
         peak, peak_kind = measured_peak()
         dominant = "quantize" if quant_ms >= deq_ms else "dequantize"
@@ -377,6 +399,8 @@ def main() -> None:
             },
             "e2e": e2e,
             "full_codec": full,
+            "config4_ragged": ragged,
+            "config5_box": box,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
@@ -385,6 +409,114 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _fits(torch, device, need_bytes: int) -> str | None:
+    """None when ``need_bytes`` (plus 2 GiB of headroom) are free on the device,
+    else the reason a leg is skipped."""
+    free, _ = torch.cuda.mem_get_info(device)
+    if free >= need_bytes + (2 << 30):
+        return None
+    return f"needs {need_bytes / 1e9:.1f} GB, {free / 1e9:.1f} GB free"
+
+
+def _timed(torch, stream, fn, iters: int):
+    """Mean device ms of ``fn`` over ``iters`` launches (CUDA events on the
+    launching stream)."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(iters):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def ragged_measure(codec, torch, layout, device, barrier, rank, world):
+    """Config 4: a 1,024-slot cache x 30 layers x 32 heads (983,040 heads,
+    64 GB fp32 + 17 GB encoded) of which 256 slots, drawn by a seeded
+    permutation of 0..1023 (int32, non-contiguous), are quantized, dequantized
+    back into the cache and projected, gathered and scattered by slot id.
+    A one-GPU configuration: under torchrun it is reported on rank 0 only."""
+    if world > 1:
+        return {"skipped": "one-GPU configuration (reported by the N=1 run)"}
+    cache_slots, active = 1024, 256
+    per_slot = LAYERS * HEADS
+    heads = active * per_slot
+    need = cache_slots * per_slot * (65536 + 16384 + 1024) + active * per_slot * (256 + 512)
+    reason = _fits(torch, device, need)
+    if reason:
+        return {"skipped": reason}
+    states = codec.synthesize_states(cache_slots, LAYERS, HEADS, layout=layout, seed=0,
+                                     device=device)
+    cache = codec.empty_encoded((cache_slots, LAYERS, HEADS), layout, device)
+    generator = torch.Generator().manual_seed(0)
+    slot_ids = torch.randperm(cache_slots, generator=generator)[:active].to(
+        torch.int32).to(device)
+    queries = codec.synthesize_queries(active, LAYERS, HEADS, seed=1, device=device)
+    outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    legs = {
+        "quantize": (lambda: codec.quantize_indexed(states, cache, slot_ids, per_slot),
+                     BYTES_PER_HEAD["quantize"]),
+        "dequantize": (lambda: codec.dequantize_indexed(cache, states, slot_ids, per_slot),
+                       BYTES_PER_HEAD["dequantize"]),
+        "projection": (lambda: codec.encoded_projection_indexed(cache, queries, slot_ids,
+                                                                per_slot, out=outputs),
+                       BYTES_PER_HEAD["projection"]),
+    }
+    for fn, _ in legs.values():
+        for _ in range(3):
+            fn()
+    barrier()
+    result = {"cache_slots": cache_slots, "active_slots": active, "heads": heads,
+              "slot_ids": "seeded permutation of 0..1023, first 256, int32"}
+    for name, (fn, per_head) in legs.items():
+        ms = _timed(torch, stream, fn, 20)
+        result[name] = {"ms": ms, "states_per_s": heads / (ms / 1e3),
+                        "gbs": per_head * heads / (ms / 1e3) / 1e9}
+    del states, cache, queries, outputs
+    return result
+
+
+def box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks, rank, world):
+    """Config 5: 2,048 request slots x 30 layers x 32 heads partitioned by slot
+    across the ranks (strong scaling, no inter-GPU traffic); one step =
+    quantize + encoded projection of every head of the rank's shard."""
+    shard = sharding.strong_shard(rank, world, 2048)
+    per_slot = LAYERS * HEADS
+    heads = shard.count * per_slot
+    need = heads * (65536 + 16384 + 1024 + 256 + 512)
+    reason = _fits(torch, device, need)
+    skipped = reason is not None
+    if world > 1:  # every rank takes the same steps: skip on all if any must
+        skipped = max_over_ranks(float(skipped)) > 0
+    if skipped:
+        return {"skipped": reason or "another rank lacks the memory"}
+    states = codec.synthesize_states(shard.count, LAYERS, HEADS, layout=layout, seed=0,
+                                     slot_base=shard.base, device=device)
+    encoded = codec.empty_encoded((shard.count, LAYERS, HEADS), layout, device)
+    queries = codec.synthesize_queries(shard.count, LAYERS, HEADS, seed=1,
+                                       slot_base=shard.base, device=device)
+    outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        codec.quantize(states, layout, out=encoded)
+        codec.encoded_projection(encoded, queries, out=outputs)
+
+    for _ in range(3):
+        step()
+    barrier()
+    iters = 10
+    ms = max_over_ranks(_timed(torch, stream, step, iters))
+    barrier()
+    per_head = BYTES_PER_HEAD["quantize"] + BYTES_PER_HEAD["projection"]
+    del states, encoded, queries, outputs
+    return {"slots": 2048, "slots_per_gpu": shard.count, "heads_per_gpu": heads,
+            "scaling": "strong", "steps": iters, "ms_per_step": ms,
+            "states_per_s": 2048 * per_slot / (ms / 1e3),
+            "hbm_gbs_per_gpu": per_head * heads / (ms / 1e3) / 1e9}
 
 
 def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank):
