@@ -29,6 +29,8 @@
 
 #include <cmath>
 
+#include <cuda_fp16.h>
+
 #include "codec_device.cuh"
 
 namespace gdnsc {
@@ -91,6 +93,106 @@ __device__ __forceinline__ bool fit_normalize(FitShared& sh, float* vec, float& 
   return true;
 }
 
+// The rank loop of QuantizeBoundary on the residual in shared memory:
+// `iterations` power sweeps per rank (the reference fixes 32), then the
+// compensators and the deflation.  Compensator keys / values of `head` go to
+// ck_out [heads][128][4] / cv_out as fp32, or rounded to binary16 when
+// kHalfOut (the window ABI's storage).  Called by all kFitThreads threads.
+template <bool kHalfOut>
+__device__ __forceinline__ void fit_ranks(FitShared& sh, int t, int iterations, uint64_t head,
+                                          void* ck_out, void* cv_out, uint32_t* status) {
+  for (int rank = 0; rank < kRank; ++rank) {
+    // -- start vector (capsule.cpp:140-144) --------------------------------
+    float rv = c_fit_sines[rank][t];
+    sh.right[t] = rv;
+    if (!fit_normalize(sh, sh.right, rv, t)) {
+      __syncthreads();
+      if (t == 0) sh.right[0] = 1.0F;
+      rv = t == 0 ? 1.0F : rv;
+    }
+    __syncthreads();
+    float lv = 0.0F;
+    for (int it = 0; it < iterations; ++it) {
+      // left[t] = sum_c R[t][c] * right[c], c = 0..127 in order.
+      {
+        float acc = 0.0F;
+        const float4* row = reinterpret_cast<const float4*>(sh.r[t]);
+        const float4* rgt = reinterpret_cast<const float4*>(sh.right);
+#pragma unroll 8
+        for (int c4 = 0; c4 < kValues / 4; ++c4) {
+          const float4 a = row[c4], b = rgt[c4];
+          acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+          acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+          acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+          acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+        }
+        lv = acc;
+        sh.left[t] = lv;
+      }
+      if (!fit_normalize(sh, sh.left, lv, t)) break;
+      __syncthreads();
+      // right[t] = sum_k R[k][t] * left[k], k = 0..127 in order.
+      {
+        float acc = 0.0F;
+#pragma unroll 8
+        for (int k = 0; k < kKeys; ++k) acc = __fadd_rn(acc, __fmul_rn(sh.r[k][t], sh.left[k]));
+        rv = acc;
+        sh.right[t] = rv;  // right[] is not read by this sweep
+      }
+      if (!fit_normalize(sh, sh.right, rv, t)) break;
+      __syncthreads();
+    }
+    __syncthreads();
+    // -- singular value: one sequential chain in row-major order -----------
+    if (t == 0) {
+      float sv = 0.0F;
+      const float4* rgt = reinterpret_cast<const float4*>(sh.right);
+      for (int k = 0; k < kKeys; ++k) {
+        const float l = sh.left[k];
+        const float4* row = reinterpret_cast<const float4*>(sh.r[k]);
+#pragma unroll 8
+        for (int c4 = 0; c4 < kValues / 4; ++c4) {
+          const float4 a = row[c4], b = rgt[c4];
+          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.x), b.x));
+          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.y), b.y));
+          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.z), b.z));
+          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.w), b.w));
+        }
+      }
+      if (!isfinite(sv)) report(status, kStatusNonFinite);
+      sh.norm = sv;
+    }
+    __syncthreads();
+    const float sv = sh.norm;
+    // -- compensators and deflation (capsule.cpp:175-187) ------------------
+    const float kl = __fmul_rn(sh.left[t], sv);
+    const uint64_t kidx = (head * kKeys + t) * kRank + rank;
+    const uint64_t vidx = (head * kValues + t) * kRank + rank;
+    if constexpr (kHalfOut) {
+      static_cast<uint16_t*>(ck_out)[kidx] = __half_as_ushort(__float2half_rn(kl));
+      static_cast<uint16_t*>(cv_out)[vidx] = __half_as_ushort(__float2half_rn(sh.right[t]));
+    } else {
+      static_cast<float*>(ck_out)[kidx] = kl;
+      static_cast<float*>(cv_out)[vidx] = sh.right[t];
+    }
+    {
+      float4* row = reinterpret_cast<float4*>(sh.r[t]);
+      const float4* rgt = reinterpret_cast<const float4*>(sh.right);
+#pragma unroll 8
+      for (int c4 = 0; c4 < kValues / 4; ++c4) {
+        float4 a = row[c4];
+        const float4 b = rgt[c4];
+        a.x = __fsub_rn(a.x, __fmul_rn(kl, b.x));
+        a.y = __fsub_rn(a.y, __fmul_rn(kl, b.y));
+        a.z = __fsub_rn(a.z, __fmul_rn(kl, b.z));
+        a.w = __fsub_rn(a.w, __fmul_rn(kl, b.w));
+        row[c4] = a;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kFitThreads) fit_kernel(FitParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   FitShared& sh = *reinterpret_cast<FitShared*>(smem_raw);
@@ -119,89 +221,8 @@ __global__ void __launch_bounds__(kFitThreads) fit_kernel(FitParams p) {
     }
     if (__syncthreads_or(!finite) != 0 && t == 0) report(p.status, kStatusNonFinite);
 
-    for (int rank = 0; rank < kRank; ++rank) {
-      // -- start vector (capsule.cpp:140-144) --------------------------------
-      float rv = c_fit_sines[rank][t];
-      sh.right[t] = rv;
-      if (!fit_normalize(sh, sh.right, rv, t)) {
-        __syncthreads();
-        if (t == 0) sh.right[0] = 1.0F;
-        rv = t == 0 ? 1.0F : rv;
-      }
-      __syncthreads();
-      float lv = 0.0F;
-      for (int it = 0; it < kFitIterations; ++it) {
-        // left[t] = sum_c R[t][c] * right[c], c = 0..127 in order.
-        {
-          float acc = 0.0F;
-          const float4* row = reinterpret_cast<const float4*>(sh.r[t]);
-          const float4* rgt = reinterpret_cast<const float4*>(sh.right);
-#pragma unroll 8
-          for (int c4 = 0; c4 < kValues / 4; ++c4) {
-            const float4 a = row[c4], b = rgt[c4];
-            acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
-            acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
-            acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
-            acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
-          }
-          lv = acc;
-          sh.left[t] = lv;
-        }
-        if (!fit_normalize(sh, sh.left, lv, t)) break;
-        __syncthreads();
-        // right[t] = sum_k R[k][t] * left[k], k = 0..127 in order.
-        {
-          float acc = 0.0F;
-#pragma unroll 8
-          for (int k = 0; k < kKeys; ++k) acc = __fadd_rn(acc, __fmul_rn(sh.r[k][t], sh.left[k]));
-          rv = acc;
-          sh.right[t] = rv;  // right[] is not read by this sweep
-        }
-        if (!fit_normalize(sh, sh.right, rv, t)) break;
-        __syncthreads();
-      }
-      __syncthreads();
-      // -- singular value: one sequential chain in row-major order -----------
-      if (t == 0) {
-        float sv = 0.0F;
-        const float4* rgt = reinterpret_cast<const float4*>(sh.right);
-        for (int k = 0; k < kKeys; ++k) {
-          const float l = sh.left[k];
-          const float4* row = reinterpret_cast<const float4*>(sh.r[k]);
-#pragma unroll 8
-          for (int c4 = 0; c4 < kValues / 4; ++c4) {
-            const float4 a = row[c4], b = rgt[c4];
-            sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.x), b.x));
-            sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.y), b.y));
-            sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.z), b.z));
-            sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.w), b.w));
-          }
-        }
-        if (!isfinite(sv)) report(p.status, kStatusNonFinite);
-        sh.norm = sv;
-      }
-      __syncthreads();
-      const float sv = sh.norm;
-      // -- compensators and deflation (capsule.cpp:175-187) ------------------
-      const float kl = __fmul_rn(sh.left[t], sv);
-      p.compensator_keys[(head * kKeys + t) * kRank + rank] = kl;
-      p.compensator_values[(head * kValues + t) * kRank + rank] = sh.right[t];
-      {
-        float4* row = reinterpret_cast<float4*>(sh.r[t]);
-        const float4* rgt = reinterpret_cast<const float4*>(sh.right);
-#pragma unroll 8
-        for (int c4 = 0; c4 < kValues / 4; ++c4) {
-          float4 a = row[c4];
-          const float4 b = rgt[c4];
-          a.x = __fsub_rn(a.x, __fmul_rn(kl, b.x));
-          a.y = __fsub_rn(a.y, __fmul_rn(kl, b.y));
-          a.z = __fsub_rn(a.z, __fmul_rn(kl, b.z));
-          a.w = __fsub_rn(a.w, __fmul_rn(kl, b.w));
-          row[c4] = a;
-        }
-      }
-      __syncthreads();
-    }
+    fit_ranks<false>(sh, t, kFitIterations, head, p.compensator_keys, p.compensator_values,
+                     p.status);
     // -- residual out, in the input's layout ---------------------------------
     float* out = p.residual + head * kElements;
     if (!p.provider) {

@@ -13,6 +13,7 @@
 #include "projection.cuh"
 #include "quantize.cuh"
 #include "synth.cuh"
+#include "window.cuh"
 #include "statecentric/gdn_state_codec_kernel.h"
 #include "statecentric/gdn_state_codec_windowed_gdn_kernel.h"
 
@@ -44,6 +45,7 @@ struct DeviceSetup {
   int dequantize_blocks[2][2] = {};
   int project_blocks[2][2] = {};
   int fit_blocks = 0;
+  WindowBlocks window;
 };
 
 std::mutex g_setup_mutex;
@@ -84,6 +86,11 @@ const DeviceSetup* device_setup() {
   }
   if (prepare_fit(&s.fit_blocks) != cudaSuccess || s.fit_blocks < 1) return nullptr;
   if (prepare_capsule() != cudaSuccess) return nullptr;
+  if (prepare_window(&s.window) != cudaSuccess || s.window.fold < 1 ||
+      s.window.dense < 1 || s.window.step[0][0] < 1 || s.window.step[0][1] < 1 ||
+      s.window.step[1][0] < 1 || s.window.step[1][1] < 1) {
+    return nullptr;
+  }
   s.ready = true;
   return &s;
 }
@@ -593,20 +600,161 @@ int32_t statecentric_gdn_state_codec_division_selftest_v1(void* stream, const fl
   return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
 }
 
-// ---- Loader-compatibility entry points (windowed decode is not implemented) -----
+// ---- Windowed decode: step, boundary refit, dense fp32 step -------------------
+
+namespace gdnsc {
+namespace {
+
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
+
+// The window buffers every step / refit reads: codes 16-byte aligned (vector
+// loads), compensators (when given) 8-byte aligned, the rest naturally.
+bool window_ok(const WindowBuffers& w, bool need_compensators) {
+  if (w.codes == nullptr || w.smoothing == nullptr || w.scales == nullptr ||
+      w.record_decay == nullptr || w.record_keys == nullptr || w.record_corrections == nullptr ||
+      w.positions == nullptr) {
+    return false;
+  }
+  if ((w.ck == nullptr) != (w.cv == nullptr)) return false;
+  if (need_compensators && w.ck == nullptr) return false;
+  if (w.ck != nullptr && (!aligned8(w.ck) || !aligned8(w.cv))) return false;
+  return aligned16(w.codes) && aligned4(w.smoothing) && aligned4(w.scales) &&
+         aligned4(w.record_decay) && aligned2(w.record_keys) && aligned2(w.record_corrections) &&
+         aligned4(w.positions);
+}
+
+int32_t run_window_step(void* stream, bool qwen, bool comp, const StepParams& p) {
+  const DeviceSetup* s = device_setup();
+  if (s == nullptr) return kSetupFailed;
+  const int grid = grid_for(p.heads, s->sms, s->window.step[qwen][comp]);
+  return launch_window_step(qwen, comp, p, grid, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? kOk
+             : kLaunchFailed;
+}
+
+}  // namespace
+}  // namespace gdnsc
 
 int32_t statecentric_gdn_state_codec_windowed_gdn_step_launch_v1(
-    void*, const int8_t*, const float*, const float*, const uint16_t*, const uint16_t*, float*,
-    uint16_t*, uint16_t*, uint32_t*, const float*, const uint16_t*, const uint16_t*,
-    const uint16_t*, const uint16_t*, float*, uint32_t) {
-  return gdnsc::kNotImplemented;
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const uint16_t* compensator_keys, const uint16_t* compensator_values, float* record_decay,
+    uint16_t* record_keys, uint16_t* record_corrections, uint32_t* positions, const float* decay,
+    const uint16_t* write_keys, const uint16_t* reads, const uint16_t* queries,
+    const uint16_t* values, float* outputs, uint32_t states) {
+  const gdnsc::WindowBuffers w{residual, smoothing, scales, compensator_keys, compensator_values,
+                               record_decay, record_keys, record_corrections, positions};
+  if (!gdnsc::window_ok(w, true) || decay == nullptr || write_keys == nullptr ||
+      reads == nullptr || queries == nullptr || values == nullptr || outputs == nullptr ||
+      states == 0u || !gdnsc::aligned4(decay) || !gdnsc::aligned2(write_keys) ||
+      !gdnsc::aligned2(reads) || !gdnsc::aligned2(queries) || !gdnsc::aligned2(values) ||
+      !gdnsc::aligned4(outputs)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::StepParams p{w, decay, nullptr, write_keys, reads, queries, values, outputs,
+                            states};
+  return gdnsc::run_window_step(stream, false, true, p);
+}
+
+namespace {
+
+int32_t window_step_bf16(void* stream, bool comp, const int8_t* residual, const float* smoothing,
+                         const float* scales, const uint16_t* compensator_keys,
+                         const uint16_t* compensator_values, float* record_decay,
+                         uint16_t* record_keys, uint16_t* record_corrections,
+                         uint32_t* positions, const float* decay, const uint16_t* beta,
+                         const uint16_t* keys, const uint16_t* queries, const uint16_t* values,
+                         uint16_t* outputs, uint32_t states) {
+  const gdnsc::WindowBuffers w{residual,     smoothing,   scales,
+                               comp ? compensator_keys : nullptr,
+                               comp ? compensator_values : nullptr,
+                               record_decay, record_keys, record_corrections, positions};
+  if ((compensator_keys == nullptr) != (compensator_values == nullptr) ||
+      !gdnsc::window_ok(w, comp) || decay == nullptr || beta == nullptr || keys == nullptr ||
+      queries == nullptr || values == nullptr || outputs == nullptr || states == 0u ||
+      states % 2u != 0u || !gdnsc::aligned4(decay) || !gdnsc::aligned2(beta) ||
+      !gdnsc::aligned2(keys) || !gdnsc::aligned2(queries) || !gdnsc::aligned2(values) ||
+      !gdnsc::aligned2(outputs)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::StepParams p{w, decay, beta, keys, nullptr, queries, values, outputs, states};
+  return gdnsc::run_window_step(stream, true, comp, p);
+}
+
+}  // namespace
+
+int32_t statecentric_gdn_state_codec_windowed_gdn_step_bf16_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const uint16_t* compensator_keys, const uint16_t* compensator_values, float* record_decay,
+    uint16_t* record_keys, uint16_t* record_corrections, uint32_t* positions, const float* decay,
+    const uint16_t* beta, const uint16_t* keys, const uint16_t* queries, const uint16_t* values,
+    uint16_t* outputs, uint32_t states) {
+  return window_step_bf16(stream, true, residual, smoothing, scales, compensator_keys,
+                          compensator_values, record_decay, record_keys, record_corrections,
+                          positions, decay, beta, keys, queries, values, outputs, states);
+}
+
+int32_t statecentric_gdn_state_codec_windowed_gdn_step_bf16_quant_only_launch_v1(
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const uint16_t* compensator_keys, const uint16_t* compensator_values, float* record_decay,
+    uint16_t* record_keys, uint16_t* record_corrections, uint32_t* positions, const float* decay,
+    const uint16_t* beta, const uint16_t* keys, const uint16_t* queries, const uint16_t* values,
+    uint16_t* outputs, uint32_t states) {
+  return window_step_bf16(stream, false, residual, smoothing, scales, compensator_keys,
+                          compensator_values, record_decay, record_keys, record_corrections,
+                          positions, decay, beta, keys, queries, values, outputs, states);
 }
 
 int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(
-    void*, const int8_t*, const float*, const float*, const uint16_t*, const uint16_t*, float*,
-    uint16_t*, uint16_t*, uint32_t*, int8_t*, float*, float*, uint16_t*, uint16_t*, float*,
-    uint32_t, uint32_t) {
-  return gdnsc::kNotImplemented;
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const uint16_t* compensator_keys, const uint16_t* compensator_values, float* record_decay,
+    uint16_t* record_keys, uint16_t* record_corrections, uint32_t* positions,
+    int8_t* next_residual, float* next_smoothing, float* next_scales,
+    uint16_t* next_compensator_keys, uint16_t* next_compensator_values, float* residual_workspace,
+    uint32_t states, uint32_t power_iterations) {
+  const gdnsc::WindowBuffers w{residual, smoothing, scales, compensator_keys, compensator_values,
+                               record_decay, record_keys, record_corrections, positions};
+  if (!gdnsc::window_ok(w, false) || next_residual == nullptr || next_smoothing == nullptr ||
+      next_scales == nullptr || next_compensator_keys == nullptr ||
+      next_compensator_values == nullptr || residual_workspace == nullptr || states == 0u ||
+      power_iterations > 32u || !aligned16(next_residual) || !aligned16(next_smoothing) ||
+      !aligned16(next_scales) || !aligned8(next_compensator_keys) ||
+      !aligned8(next_compensator_values) || !aligned16(residual_workspace)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const gdnsc::FoldParams fp{w, next_compensator_keys, next_compensator_values,
+                             residual_workspace, states, static_cast<int>(power_iterations)};
+  if (gdnsc::launch_window_fold(fp, gdnsc::grid_for(states, s->sms, s->window.fold), st) !=
+      cudaSuccess) {
+    return gdnsc::kLaunchFailed;
+  }
+  return gdnsc::run_quantize(stream, true, gdnsc::kFused, residual_workspace, nullptr,
+                             next_smoothing, next_residual, next_scales, states,
+                             SlotMap{nullptr, 1, 1}, nullptr);
+}
+
+int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
+    void* stream, float* dense_state, const float* decay, const uint16_t* key,
+    const uint16_t* read, const uint16_t* query, const uint16_t* value, float* output,
+    uint32_t states) {
+  if (dense_state == nullptr || decay == nullptr || key == nullptr || read == nullptr ||
+      query == nullptr || value == nullptr || output == nullptr || states == 0u ||
+      !gdnsc::aligned4(dense_state) || !gdnsc::aligned4(decay) || !gdnsc::aligned2(key) ||
+      !gdnsc::aligned2(read) || !gdnsc::aligned2(query) || !gdnsc::aligned2(value) ||
+      !gdnsc::aligned4(output)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  const gdnsc::DenseStepParams p{dense_state, decay, key, read, query, value, output, states};
+  return gdnsc::launch_dense_step(p, gdnsc::grid_for(states, s->sms, s->window.dense),
+                                  static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? gdnsc::kOk
+             : gdnsc::kLaunchFailed;
 }
 
 }  // extern "C"

@@ -1,0 +1,509 @@
+// window.cuh -- the p = 16 windowed decode step, its boundary refit and the
+// dense fp32 GDN step (sm_100a).
+//
+// A head's decode state is the INT8 boundary (codes, smoothing c, scales b,
+// binary16 rank-4 compensators) plus up to 16 buffered rank-one records
+// {decay, key, correction} (record_decay fp32 [16], record_keys /
+// record_corrections binary16 [16][128], position u32 at [head][8]), the
+// buffers of gdn_state_codec_windowed_gdn_kernel.h:5-6.
+//
+// Step (capsule.cpp:354-397, ApplyToken, with the read of :256-304):
+//   state_read = Read(read);  correction = value - state_read
+//   output     = Read(decay * query) + correction * (key . query)
+//   append {decay, key, correction}; position += 1
+// where Read(x)[v] walks the records newest first (projection of the
+// suffix-decayed x onto the record key, times the record correction, then
+// x *= record decay), then adds the boundary readout
+// (sum_k (z[k][v] c_k) x_k, k in order) / 127 * b_v and the compensators
+// V[v][r] (sum_k K[k][r] x_k).  Every sum keeps the reference's sequential
+// order and every product is rounded before its add (__fmul_rn / __fadd_rn),
+// so outputs and records are bit-identical to the portable library's
+// arithmetic with the ABI's binary16 record storage.
+//
+// Qwen3.5 form (the vLLM plugin's decode, runtime.py:750-845): decay =
+// exp(log decay), key = beta k, read = decay k, query = 128^-0.5 q, with q / k
+// of head h taken from head h / 2 (two value heads per query/key head) and a
+// bf16 output; boundary codes in the provider layout [v][k].  Generic form
+// (windowed_gdn_step_launch_v1): decay, write key, read, query and value
+// given directly (binary16), fp32 output, capsule-layout codes [k][v].
+//
+// Design: one 128-thread CTA per head, persistent over heads.  Thread t owns
+// key t for the vector work and value column t for the readout.  The suffix-
+// decayed read vectors live in shared memory (rows padded to 129 floats so
+// the per-record projections, one thread per (record, read), are conflict-
+// free); those projections and the compensator / update projections run on
+// the first warps while every thread sums its column's boundary readout for
+// both reads at once with packed fp32x2 arithmetic.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "codec_device.cuh"
+#include "fit.cuh"
+
+namespace gdnsc {
+
+constexpr int kWindow = 16;                 // capsule.h:14, p = 16
+constexpr int kPositionStride = 8;          // positions [head][8]
+constexpr int kWinThreads = 128;
+constexpr uint32_t kStatusWindowFull = 8u;  // a step found a head's window full
+constexpr float kQueryScale = 0.08838834764831845F;  // 128^-0.5 (windowed_gdn_step.cpp:297)
+
+struct WindowBuffers {
+  const int8_t* codes;             // [heads][128][128]
+  const float* smoothing;          // [heads][128]
+  const float* scales;             // [heads][128]
+  const uint16_t* ck;              // binary16 [heads][128][4] or nullptr (none)
+  const uint16_t* cv;              // binary16 [heads][128][4] or nullptr
+  float* record_decay;             // [heads][16]
+  uint16_t* record_keys;           // binary16 [heads][16][128]
+  uint16_t* record_corrections;    // binary16 [heads][16][128]
+  uint32_t* positions;             // [heads][8], position at [head][0]
+};
+
+struct StepParams {
+  WindowBuffers w;
+  const float* decay;        // Qwen: log decay [heads]; generic: decay [heads]
+  const uint16_t* beta;      // Qwen: bf16 [heads]
+  const uint16_t* keys;      // Qwen: bf16 [heads/2][128]; generic: binary16 write keys [heads][128]
+  const uint16_t* reads;     // generic: binary16 [heads][128]
+  const uint16_t* queries;   // Qwen: bf16 [heads/2][128]; generic: binary16 [heads][128]
+  const uint16_t* values;    // Qwen: bf16 [heads][128]; generic: binary16 [heads][128]
+  void* outputs;             // Qwen: bf16 [heads][128]; generic: fp32 [heads][128]
+  uint64_t heads;
+};
+
+struct __align__(16) StepShared {
+  float suffix[2][kWindow][kKeys + 1];  // suffix-decayed read / query before record p-1-j
+  float rkey[kWindow][kKeys + 1];       // record keys (fp32)
+  float2 sfinal[kKeys];                 // (read, query) suffix after every record
+  float4 ck[kKeys];                     // compensator keys
+  float c[kKeys];                       // smoothing
+  float key[kKeys];                     // write key of this token
+  float query[kKeys];                   // query of this token (undecayed)
+  float proj[2][kWindow];               // record projections per read
+  float cproj[2][kRank];                // compensator projections per read
+  float up;                             // key . query
+};
+
+struct __align__(16) StepSharedCapsule {
+  StepShared s;
+  int8_t codes[kElements];  // capsule-layout codes staged for column reads
+};
+
+__device__ __forceinline__ float half_to_float(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ float bf16_to_float(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+__device__ __forceinline__ uint16_t float_to_half_bits(float x) {
+  return __half_as_ushort(__float2half_rn(x));
+}
+
+// One sequential dot product sum_k a[k * sa] * b[k * sb], k = 0..127.
+__device__ __forceinline__ float chain_dot(const float* a, int sa, const float* b, int sb) {
+  float acc = 0.0F;
+#pragma unroll 8
+  for (int k = 0; k < kKeys; ++k) acc = __fadd_rn(acc, __fmul_rn(a[k * sa], b[k * sb]));
+  return acc;
+}
+
+template <bool kQwen, bool kComp>
+__global__ void __launch_bounds__(kWinThreads) window_step_kernel(StepParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  StepShared& sh = *reinterpret_cast<StepShared*>(smem_raw);
+  const int t = threadIdx.x;
+  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    const uint32_t pos = __ldcg(p.w.positions + head * kPositionStride);
+    if (pos >= kWindow) {  // block-uniform: every thread read the same word
+      if (t == 0) report(nullptr, kStatusWindowFull);
+      continue;
+    }
+    const int np = static_cast<int>(pos);
+    // ---- codes of column t (provider: one 128-byte row per value) ---------
+    uint4 zrow[8];
+    if constexpr (kQwen) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.w.codes + head * kElements + t * kKeys);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) zrow[i] = __ldcs(src + i);
+    } else {
+      int8_t* staged = reinterpret_cast<StepSharedCapsule*>(smem_raw)->codes;
+      const uint4* src = reinterpret_cast<const uint4*>(p.w.codes + head * kElements);
+#pragma unroll
+      for (int i = 0; i < kElements / 16 / kWinThreads; ++i) {
+        reinterpret_cast<uint4*>(staged)[t + kWinThreads * i] = __ldcs(src + t + kWinThreads * i);
+      }
+    }
+    // ---- token inputs (thread t: key t and value t) -----------------------
+    float alpha, key_t, read_t, query_t, value_t;
+    if constexpr (kQwen) {
+      alpha = expf(__ldg(p.decay + head));
+      const float beta = bf16_to_float(__ldg(p.beta + head));
+      const uint64_t qk = (head >> 1) * kKeys + t;
+      const float k = bf16_to_float(__ldg(p.keys + qk));
+      key_t = __fmul_rn(beta, k);
+      read_t = __fmul_rn(alpha, k);
+      query_t = __fmul_rn(kQueryScale, bf16_to_float(__ldg(p.queries + qk)));
+      value_t = bf16_to_float(__ldg(p.values + head * kValues + t));
+    } else {
+      alpha = __ldg(p.decay + head);
+      key_t = half_to_float(__ldg(p.keys + head * kKeys + t));
+      read_t = half_to_float(__ldg(p.reads + head * kKeys + t));
+      query_t = half_to_float(__ldg(p.queries + head * kKeys + t));
+      value_t = half_to_float(__ldg(p.values + head * kValues + t));
+    }
+    sh.key[t] = key_t;
+    sh.query[t] = query_t;
+    sh.c[t] = __ldg(p.w.smoothing + head * kKeys + t);
+    const float b_t = __ldg(p.w.scales + head * kValues + t);
+    float cv_t[kRank] = {0.F, 0.F, 0.F, 0.F};
+    if constexpr (kComp) {
+      const uint2 kw = __ldg(reinterpret_cast<const uint2*>(p.w.ck + (head * kKeys + t) * kRank));
+      sh.ck[t] = make_float4(half_to_float(kw.x & 0xFFFFu), half_to_float(kw.x >> 16),
+                             half_to_float(kw.y & 0xFFFFu), half_to_float(kw.y >> 16));
+      const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
+      cv_t[0] = half_to_float(vw.x & 0xFFFFu);
+      cv_t[1] = half_to_float(vw.x >> 16);
+      cv_t[2] = half_to_float(vw.y & 0xFFFFu);
+      cv_t[3] = half_to_float(vw.y >> 16);
+    }
+    // ---- records: keys to shared memory, corrections of column t ----------
+    const uint64_t rbase = head * kWindow;
+    float rc[kWindow];
+#pragma unroll
+    for (int u = 0; u < kWindow; ++u) {
+      rc[u] = 0.0F;
+      if (u < np) {
+        sh.rkey[u][t] = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + t));
+        rc[u] = half_to_float(__ldcg(p.w.record_corrections + (rbase + u) * kValues + t));
+      }
+    }
+    // ---- suffix-decayed read and query (thread t = key t) -----------------
+    {
+      float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
+      for (int j = 0; j < np; ++j) {  // record np-1-j is read with suffix j
+        sh.suffix[0][j][t] = s0;
+        sh.suffix[1][j][t] = s1;
+        const float d = __ldcg(p.w.record_decay + rbase + (np - 1 - j));
+        s0 = __fmul_rn(s0, d);
+        s1 = __fmul_rn(s1, d);
+      }
+      sh.sfinal[t] = make_float2(s0, s1);
+    }
+    __syncthreads();
+    // ---- sequential projections: records, compensators, update -----------
+    const int chains = 2 * np + (kComp ? 2 * kRank : 0) + 1;
+    if (t < chains) {
+      const float* a;
+      const float* b;
+      int sa = 1, sb = 1;
+      float* dst;
+      if (t < 2 * np) {
+        const int r = t / np == 0 ? 0 : 1;
+        const int u = t - r * np;
+        a = &sh.rkey[u][0];
+        b = &sh.suffix[r][np - 1 - u][0];
+        dst = &sh.proj[r][u];
+      } else if (kComp && t < 2 * np + 2 * kRank) {
+        const int i = t - 2 * np;
+        const int r = i / kRank, m = i % kRank;
+        a = reinterpret_cast<const float*>(sh.ck) + m;
+        sa = 4;
+        b = reinterpret_cast<const float*>(sh.sfinal) + r;
+        sb = 2;
+        dst = &sh.cproj[r][m];
+      } else {
+        a = sh.key;
+        b = sh.query;
+        dst = &sh.up;
+      }
+      *dst = chain_dot(a, sa, b, sb);
+    }
+    // ---- boundary readout of column t for both reads ----------------------
+    f2 acc = pack2(0.0F, 0.0F);
+    const f2* sf = reinterpret_cast<const f2*>(sh.sfinal);
+    if constexpr (kQwen) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t words[4] = {zrow[i].x, zrow[i].y, zrow[i].z, zrow[i].w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int k0 = 16 * i + 4 * w;
+          f2 z01, z23;
+          unpack_codes(words[w], z01, z23);
+          const f2 zc01 = mul2(z01, *reinterpret_cast<const f2*>(&sh.c[k0]));
+          const f2 zc23 = mul2(z23, *reinterpret_cast<const f2*>(&sh.c[k0 + 2]));
+          acc = add2(acc, mul2_for_add(pack2(lo2(zc01), lo2(zc01)), sf[k0]));
+          acc = add2(acc, mul2_for_add(pack2(hi2(zc01), hi2(zc01)), sf[k0 + 1]));
+          acc = add2(acc, mul2_for_add(pack2(lo2(zc23), lo2(zc23)), sf[k0 + 2]));
+          acc = add2(acc, mul2_for_add(pack2(hi2(zc23), hi2(zc23)), sf[k0 + 3]));
+        }
+      }
+    } else {
+      const int8_t* staged = reinterpret_cast<StepSharedCapsule*>(smem_raw)->codes;
+#pragma unroll 8
+      for (int k = 0; k < kKeys; ++k) {
+        const float zc = __fmul_rn(static_cast<float>(staged[k * kValues + t]), sh.c[k]);
+        acc = add2(acc, mul2_for_add(pack2(zc, zc), sf[k]));
+      }
+    }
+    __syncthreads();
+    // ---- column t: records newest first, boundary, compensators -----------
+    float out0 = 0.0F, out1 = 0.0F;
+#pragma unroll
+    for (int u = kWindow - 1; u >= 0; --u) {
+      if (u < np) {
+        out0 = __fadd_rn(out0, __fmul_rn(rc[u], sh.proj[0][u]));
+        out1 = __fadd_rn(out1, __fmul_rn(rc[u], sh.proj[1][u]));
+      }
+    }
+    out0 = __fadd_rn(out0, __fmul_rn(div127_any(lo2(acc)), b_t));
+    out1 = __fadd_rn(out1, __fmul_rn(div127_any(hi2(acc)), b_t));
+    if constexpr (kComp) {
+#pragma unroll
+      for (int m = 0; m < kRank; ++m) {
+        out0 = __fadd_rn(out0, __fmul_rn(cv_t[m], sh.cproj[0][m]));
+        out1 = __fadd_rn(out1, __fmul_rn(cv_t[m], sh.cproj[1][m]));
+      }
+    }
+    const float correction = __fsub_rn(value_t, out0);
+    const float output = __fadd_rn(out1, __fmul_rn(correction, sh.up));
+    if constexpr (kQwen) {
+      static_cast<uint16_t*>(p.outputs)[head * kValues + t] =
+          __bfloat16_as_ushort(__float2bfloat16_rn(output));
+    } else {
+      static_cast<float*>(p.outputs)[head * kValues + t] = output;
+    }
+    if (!isfinite(output)) report(nullptr, kStatusNonFinite);
+    // ---- append the record -------------------------------------------------
+    p.w.record_keys[(rbase + np) * kKeys + t] = float_to_half_bits(key_t);
+    p.w.record_corrections[(rbase + np) * kValues + t] = float_to_half_bits(correction);
+    if (t == 0) {
+      p.w.record_decay[rbase + np] = alpha;
+      p.w.positions[head * kPositionStride] = pos + 1u;
+    }
+    __syncthreads();  // shared memory is reused by the next head
+  }
+}
+
+template <bool kQwen>
+inline size_t window_step_smem_bytes() {
+  return kQwen ? sizeof(StepShared) : sizeof(StepSharedCapsule);
+}
+
+// ---------------------------------------------------------------------------
+// Boundary refit (window_boundary_launch_v1): DenseState of the window
+// (capsule.cpp:337-352, dequantized boundary then every record oldest first)
+// into shared memory, QuantizeBoundary's rank loop with `iterations` power
+// sweeps (none: quant-only refit, zero compensators), the residual written to
+// the caller's workspace in the provider layout for the INT8 stage that
+// follows, and the window cleared (records zero, position 0).
+
+struct FoldParams {
+  WindowBuffers w;           // current boundary and records (records cleared)
+  uint16_t* next_ck;         // binary16 [heads][128][4]
+  uint16_t* next_cv;         // binary16 [heads][128][4]
+  float* workspace;          // [heads][128][128] residual, provider layout
+  uint64_t heads;
+  int iterations;            // 0..32
+};
+
+struct __align__(16) FoldExtra {
+  float rc[kWindow][kValues];   // record corrections
+  float4 cv[kValues];           // compensator values
+  float b[kValues];             // scales
+};
+
+__global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  FitShared& sh = *reinterpret_cast<FitShared*>(smem_raw);
+  FoldExtra& ex = *reinterpret_cast<FoldExtra*>(smem_raw + ((sizeof(FitShared) + 15) & ~size_t{15}));
+  const int t = threadIdx.x;
+  const bool comp = p.w.ck != nullptr;
+  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
+    const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
+    const uint64_t rbase = head * kWindow;
+    // ---- gather the window (thread t: key t, value t) ----------------------
+    ex.b[t] = __ldg(p.w.scales + head * kValues + t);
+    float4 ck_t = make_float4(0.F, 0.F, 0.F, 0.F);
+    if (comp) {
+      const uint2 kw = __ldg(reinterpret_cast<const uint2*>(p.w.ck + (head * kKeys + t) * kRank));
+      ck_t = make_float4(half_to_float(kw.x & 0xFFFFu), half_to_float(kw.x >> 16),
+                         half_to_float(kw.y & 0xFFFFu), half_to_float(kw.y >> 16));
+      const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
+      ex.cv[t] = make_float4(half_to_float(vw.x & 0xFFFFu), half_to_float(vw.x >> 16),
+                             half_to_float(vw.y & 0xFFFFu), half_to_float(vw.y >> 16));
+    }
+    float rk[kWindow], rd[kWindow];
+#pragma unroll
+    for (int u = 0; u < kWindow; ++u) {
+      rk[u] = 0.0F;
+      rd[u] = 0.0F;
+      if (u < np) {
+        rk[u] = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + t));
+        rd[u] = __ldcg(p.w.record_decay + rbase + u);
+        ex.rc[u][t] = half_to_float(__ldcg(p.w.record_corrections + (rbase + u) * kValues + t));
+      }
+    }
+    const float c_t = __ldg(p.w.smoothing + head * kKeys + t);
+    __syncthreads();
+    // ---- dense[t][v]: boundary, compensators, records oldest first ---------
+    bool finite = true;
+    const int8_t* codes = p.w.codes + head * kElements;
+    for (int v = 0; v < kValues; ++v) {
+      const float z = static_cast<float>(__ldg(codes + v * kKeys + t));  // provider [v][k]
+      float value = __fmul_rn(div127_any(__fmul_rn(c_t, z)), ex.b[v]);
+      if (comp) {
+        const float4 cvv = ex.cv[v];
+        value = __fadd_rn(value, __fmul_rn(ck_t.x, cvv.x));
+        value = __fadd_rn(value, __fmul_rn(ck_t.y, cvv.y));
+        value = __fadd_rn(value, __fmul_rn(ck_t.z, cvv.z));
+        value = __fadd_rn(value, __fmul_rn(ck_t.w, cvv.w));
+      }
+#pragma unroll
+      for (int u = 0; u < kWindow; ++u) {
+        if (u < np) value = __fadd_rn(__fmul_rn(rd[u], value), __fmul_rn(rk[u], ex.rc[u][v]));
+      }
+      finite = finite && isfinite(value);
+      sh.r[t][v] = value;
+    }
+    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
+    // ---- the window is folded: clear it (every read of it is done) ---------
+#pragma unroll 4
+    for (int u = 0; u < kWindow; ++u) {
+      p.w.record_keys[(rbase + u) * kKeys + t] = 0;
+      p.w.record_corrections[(rbase + u) * kValues + t] = 0;
+    }
+    if (t < kWindow) p.w.record_decay[rbase + t] = 0.0F;
+    if (t == 0) p.w.positions[head * kPositionStride] = 0u;
+    // ---- rank-4 fit, or zero compensators for the quant-only refit ---------
+    if (p.iterations > 0) {
+      fit_ranks<true>(sh, t, p.iterations, head, p.next_ck, p.next_cv, nullptr);
+    } else {
+      reinterpret_cast<uint2*>(p.next_ck + (head * kKeys + t) * kRank)[0] = make_uint2(0u, 0u);
+      reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
+    }
+    // ---- residual to the workspace, provider layout [v][k] -----------------
+    float* out = p.workspace + head * kElements;
+    for (int v = 0; v < kValues; ++v) __stcg(out + v * kKeys + t, sh.r[t][v]);
+    __syncthreads();  // the next head overwrites shared memory
+  }
+}
+
+inline size_t window_fold_smem_bytes() {
+  return ((sizeof(FitShared) + 15) & ~size_t{15}) + sizeof(FoldExtra);
+}
+
+// ---------------------------------------------------------------------------
+// Dense fp32 GDN step (fp32_gdn_step_launch_v1; reference kernel
+// native/ascendc/gdn_state_codec/kernel/gdn_state_codec_fp32_gdn_step.cpp:
+// 10-16), in place on capsule-layout [k][v] states: per value column v,
+// correction = value[v] - sum_k S[k][v] read[k]; S[k][v] = decay S[k][v] +
+// key[k] correction; out[v] = sum_k S_new[k][v] query[k] (k in order).
+
+struct DenseStepParams {
+  float* state;              // [heads][128][128] capsule layout, updated in place
+  const float* decay;        // [heads]
+  const uint16_t* keys;      // binary16 [heads][128]
+  const uint16_t* reads;
+  const uint16_t* queries;
+  const uint16_t* values;
+  float* outputs;            // [heads][128]
+  uint64_t heads;
+};
+
+__global__ void __launch_bounds__(kWinThreads) dense_step_kernel(DenseStepParams p) {
+  __shared__ float key[kKeys], read[kKeys], query[kKeys];
+  const int t = threadIdx.x;
+  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    key[t] = half_to_float(__ldg(p.keys + head * kKeys + t));
+    read[t] = half_to_float(__ldg(p.reads + head * kKeys + t));
+    query[t] = half_to_float(__ldg(p.queries + head * kKeys + t));
+    const float value = half_to_float(__ldg(p.values + head * kValues + t));
+    const float decay = __ldg(p.decay + head);
+    __syncthreads();
+    float* s = p.state + head * kElements + t;
+    float projection = 0.0F;
+#pragma unroll 8
+    for (int k = 0; k < kKeys; ++k) projection = __fadd_rn(projection, __fmul_rn(s[k * kValues], read[k]));
+    const float correction = __fsub_rn(value, projection);
+    float out = 0.0F;
+#pragma unroll 8
+    for (int k = 0; k < kKeys; ++k) {
+      const float next = __fadd_rn(__fmul_rn(decay, s[k * kValues]), __fmul_rn(key[k], correction));
+      s[k * kValues] = next;
+      out = __fadd_rn(out, __fmul_rn(next, query[k]));
+    }
+    p.outputs[head * kValues + t] = out;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host set-up and launches.
+
+struct WindowBlocks {
+  int step[2][2] = {};  // [qwen][comp] blocks per SM
+  int fold = 0;
+  int dense = 0;
+};
+
+template <bool kQwen, bool kComp>
+inline cudaError_t prepare_step_variant(int* blocks) {
+  const auto kernel = window_step_kernel<kQwen, kComp>;
+  const size_t smem = window_step_smem_bytes<kQwen>();
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, kWinThreads, smem);
+}
+
+inline cudaError_t prepare_window(WindowBlocks* b) {
+  cudaError_t err;
+  if ((err = prepare_step_variant<true, true>(&b->step[1][1])) != cudaSuccess) return err;
+  if ((err = prepare_step_variant<true, false>(&b->step[1][0])) != cudaSuccess) return err;
+  if ((err = prepare_step_variant<false, true>(&b->step[0][1])) != cudaSuccess) return err;
+  if ((err = prepare_step_variant<false, false>(&b->step[0][0])) != cudaSuccess) return err;
+  err = cudaFuncSetAttribute(window_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(window_fold_smem_bytes()));
+  if (err != cudaSuccess) return err;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->fold, window_fold_kernel, kFitThreads,
+                                                      window_fold_smem_bytes());
+  if (err != cudaSuccess) return err;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->dense, dense_step_kernel, kWinThreads, 0);
+}
+
+inline cudaError_t launch_window_step(bool qwen, bool comp, const StepParams& p, int grid,
+                                      cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWinThreads);
+  cfg.stream = stream;
+  if (qwen) {
+    cfg.dynamicSmemBytes = window_step_smem_bytes<true>();
+    return comp ? cudaLaunchKernelEx(&cfg, window_step_kernel<true, true>, p)
+                : cudaLaunchKernelEx(&cfg, window_step_kernel<true, false>, p);
+  }
+  cfg.dynamicSmemBytes = window_step_smem_bytes<false>();
+  return comp ? cudaLaunchKernelEx(&cfg, window_step_kernel<false, true>, p)
+              : cudaLaunchKernelEx(&cfg, window_step_kernel<false, false>, p);
+}
+
+inline cudaError_t launch_window_fold(const FoldParams& p, int grid, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFitThreads);
+  cfg.dynamicSmemBytes = window_fold_smem_bytes();
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, window_fold_kernel, p);
+}
+
+inline cudaError_t launch_dense_step(const DenseStepParams& p, int grid, cudaStream_t stream) {
+  dense_step_kernel<<<grid, kWinThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace gdnsc

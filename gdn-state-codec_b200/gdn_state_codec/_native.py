@@ -62,9 +62,13 @@ SIGNATURES: dict[str, list] = {
     "statecentric_gdn_state_codec_synthesize_queries_v1":
         [_vp, _vp, _u64, _u32, _u32, _u32, _u32],
     "statecentric_gdn_state_codec_division_selftest_v1": [_vp, _vp, _vp, _vp, _u64],
-    # loader-compatibility entry points (windowed decode not implemented)
+    # windowed decode (gdn_state_codec_windowed_gdn_kernel.h)
     "statecentric_gdn_state_codec_windowed_gdn_step_launch_v1": [_vp] * 16 + [_u32],
+    "statecentric_gdn_state_codec_windowed_gdn_step_bf16_launch_v1": [_vp] * 16 + [_u32],
+    "statecentric_gdn_state_codec_windowed_gdn_step_bf16_quant_only_launch_v1":
+        [_vp] * 16 + [_u32],
     "statecentric_gdn_state_codec_window_boundary_launch_v1": [_vp] * 16 + [_u32, _u32],
+    "statecentric_gdn_state_codec_fp32_gdn_step_launch_v1": [_vp] * 8 + [_u32],
 }
 
 _lock = threading.Lock()

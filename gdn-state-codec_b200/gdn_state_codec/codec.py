@@ -63,7 +63,7 @@ def _check(tensor: torch.Tensor, name: str, dtype: torch.dtype, last: tuple[int,
         raise ValueError(f"{name} must be {dtype} (got {tensor.dtype})")
     if not tensor.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
-    if tensor.dim() < len(last) or tuple(tensor.shape[-len(last):]) != last:
+    if last and (tensor.dim() < len(last) or tuple(tensor.shape[-len(last):]) != last):
         raise ValueError(f"{name} must end in shape {last} (got {tuple(tensor.shape)})")
     count = 1
     for size in tensor.shape[: tensor.dim() - len(last)]:
@@ -453,6 +453,217 @@ def encoded_projection_indexed(encoded_cache: EncodedStates, queries: torch.Tens
             _ptr(encoded_cache.smoothing), _ptr(encoded_cache.scales), _ptr(ck), _ptr(cv),
             _ptr(queries), _ptr(out), _ptr(slot_ids), count, heads_per_slot, num_slots,
             _ptr(status)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Windowed decode (p = 16 records over the INT8 boundary).
+
+WINDOW_SIZE = 16
+POSITION_STRIDE = 8
+STATUS_WINDOW_FULL = 8
+
+
+@dataclass
+class WindowStates:
+    """Encoded heads with their decode windows (the window ABI's buffers):
+    the INT8 boundary, binary16 rank-4 compensators (None: quant-only
+    boundary), and per head up to 16 records {decay fp32, key fp16 [128],
+    correction fp16 [128]} with the window position in ``positions[..., 0]``."""
+
+    encoded: EncodedStates
+    compensator_keys: torch.Tensor | None
+    compensator_values: torch.Tensor | None
+    record_decay: torch.Tensor
+    record_keys: torch.Tensor
+    record_corrections: torch.Tensor
+    positions: torch.Tensor
+
+    @property
+    def heads(self) -> int:
+        return self.encoded.heads
+
+
+def new_window(encoded: EncodedStates, compensator_keys: torch.Tensor | None = None,
+               compensator_values: torch.Tensor | None = None) -> WindowStates:
+    """An empty window (position 0) over ``encoded``; compensators are
+    binary16 [..., 128, 4] or None."""
+    heads = _check_encoded(encoded)
+    device = encoded.codes.device
+    if (compensator_keys is None) != (compensator_values is None):
+        raise ValueError("compensator_keys and compensator_values go together")
+    if compensator_keys is not None:
+        if (_check(compensator_keys, "compensator_keys", torch.float16,
+                   (KEY_DIMENSION, COMPENSATOR_RANK), device) != heads or
+                _check(compensator_values, "compensator_values", torch.float16,
+                       (VALUE_DIMENSION, COMPENSATOR_RANK), device) != heads):
+            raise ValueError("compensators must have one [128, 4] block per state")
+    shape = tuple(encoded.codes.shape[:-2])
+    return WindowStates(
+        encoded, compensator_keys, compensator_values,
+        record_decay=torch.zeros((*shape, WINDOW_SIZE), dtype=torch.float32, device=device),
+        record_keys=torch.zeros((*shape, WINDOW_SIZE, KEY_DIMENSION), dtype=torch.float16,
+                                device=device),
+        record_corrections=torch.zeros((*shape, WINDOW_SIZE, VALUE_DIMENSION),
+                                       dtype=torch.float16, device=device),
+        positions=torch.zeros((*shape, POSITION_STRIDE), dtype=torch.int32, device=device))
+
+
+def _check_window(window: WindowStates) -> int:
+    heads = _check_encoded(window.encoded)
+    dev = window.encoded.codes.device
+    if window.compensator_keys is not None:
+        if (_check(window.compensator_keys, "compensator_keys", torch.float16,
+                   (KEY_DIMENSION, COMPENSATOR_RANK), dev) != heads or
+                _check(window.compensator_values, "compensator_values", torch.float16,
+                       (VALUE_DIMENSION, COMPENSATOR_RANK), dev) != heads):
+            raise ValueError("compensators must have one [128, 4] block per state")
+    for tensor, name, dtype, last in (
+            (window.record_decay, "record_decay", torch.float32, (WINDOW_SIZE,)),
+            (window.record_keys, "record_keys", torch.float16, (WINDOW_SIZE, KEY_DIMENSION)),
+            (window.record_corrections, "record_corrections", torch.float16,
+             (WINDOW_SIZE, VALUE_DIMENSION)),
+            (window.positions, "positions", torch.int32, (POSITION_STRIDE,))):
+        if _check(tensor, name, dtype, last, dev) != heads:
+            raise ValueError(f"{name} must have one block per state")
+    return heads
+
+
+def _window_args(window: WindowStates):
+    return (_ptr(window.encoded.codes), _ptr(window.encoded.smoothing),
+            _ptr(window.encoded.scales), _ptr(window.compensator_keys),
+            _ptr(window.compensator_values), _ptr(window.record_decay),
+            _ptr(window.record_keys), _ptr(window.record_corrections), _ptr(window.positions))
+
+
+def _vectors(heads: int, device, dtype, shapes: dict) -> None:
+    for name, (tensor, count) in shapes.items():
+        if _check(tensor, name, dtype, (KEY_DIMENSION,), device) != count:
+            raise ValueError(f"{name} must be [{count}, 128] {dtype}")
+
+
+def window_step_bf16(window: WindowStates, log_decay: torch.Tensor, beta: torch.Tensor,
+                     keys: torch.Tensor, queries: torch.Tensor, values: torch.Tensor, *,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """One Qwen3.5 decode token for every head (ApplyToken, capsule.cpp:354-397):
+    log_decay fp32 [H], beta bf16 [H], keys / queries bf16 [H/2, 128] (value
+    heads 2j, 2j+1 share query/key head j), values bf16 [H, 128]; returns the
+    bf16 outputs [H, 128] and appends one record per head.  The boundary must
+    be provider layout.  Quant-only windows (no compensators) use the
+    quant-only kernel."""
+    heads = _check_window(window)
+    device = window.encoded.codes.device
+    if window.encoded.layout != "provider":
+        raise ValueError("the bf16 decode step reads provider-layout boundaries")
+    if heads % 2:
+        raise ValueError("the bf16 decode step needs an even number of heads")
+    if _check(log_decay, "log_decay", torch.float32, (), device) != heads or \
+            _check(beta, "beta", torch.bfloat16, (), device) != heads:
+        raise ValueError("log_decay and beta must hold one value per head")
+    _vectors(heads, device, torch.bfloat16, {"keys": (keys, heads // 2),
+                                             "queries": (queries, heads // 2),
+                                             "values": (values, heads)})
+    if out is None:
+        out = torch.empty((heads, VALUE_DIMENSION), dtype=torch.bfloat16, device=device)
+    _vectors(heads, device, torch.bfloat16, {"outputs": (out, heads)})
+    quant_only = window.compensator_keys is None
+    name = ("windowed_gdn_step_bf16_quant_only_launch_v1" if quant_only
+            else "windowed_gdn_step_bf16_launch_v1")
+    with torch.cuda.device(device):
+        _status("decode step", _native.call(
+            "statecentric_gdn_state_codec_" + name, _stream(device), *_window_args(window),
+            _ptr(log_decay), _ptr(beta), _ptr(keys), _ptr(queries), _ptr(values), _ptr(out),
+            heads))
+    return out
+
+
+def window_step(window: WindowStates, decay: torch.Tensor, write_keys: torch.Tensor,
+                reads: torch.Tensor, queries: torch.Tensor, values: torch.Tensor, *,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """The generic decode step (windowed_gdn_step_launch_v1): decay fp32 [H]
+    and fp16 [H, 128] write keys, reads, queries and values; fp32 outputs.
+    The boundary must be capsule layout and carry compensators."""
+    heads = _check_window(window)
+    device = window.encoded.codes.device
+    if window.encoded.layout != "capsule":
+        raise ValueError("the generic decode step reads capsule-layout boundaries")
+    if window.compensator_keys is None:
+        raise ValueError("the generic decode step needs compensators")
+    if _check(decay, "decay", torch.float32, (), device) != heads:
+        raise ValueError("decay must hold one value per head")
+    _vectors(heads, device, torch.float16, {"write_keys": (write_keys, heads),
+                                            "reads": (reads, heads),
+                                            "queries": (queries, heads),
+                                            "values": (values, heads)})
+    if out is None:
+        out = torch.empty((heads, VALUE_DIMENSION), dtype=torch.float32, device=device)
+    _vectors(heads, device, torch.float32, {"outputs": (out, heads)})
+    with torch.cuda.device(device):
+        _status("decode step", _native.call(
+            "statecentric_gdn_state_codec_windowed_gdn_step_launch_v1", _stream(device),
+            *_window_args(window), _ptr(decay), _ptr(write_keys), _ptr(reads), _ptr(queries),
+            _ptr(values), _ptr(out), heads))
+    return out
+
+
+def window_refit(window: WindowStates, power_iterations: int = 0, *,
+                 workspace: torch.Tensor | None = None) -> WindowStates:
+    """Fold every head's window into a new boundary (DenseState then
+    QuantizeBoundary with ``power_iterations`` sweeps per rank; 0 = quant-only
+    boundary with zero compensators).  The records of ``window`` are cleared
+    in place; the returned WindowStates holds the new boundary and shares the
+    record buffers.  A quant-only window refit without power iterations stays
+    quant-only (no compensators)."""
+    heads = _check_window(window)
+    device = window.encoded.codes.device
+    if window.encoded.layout != "provider":
+        raise ValueError("the boundary refit reads provider-layout boundaries")
+    if not 0 <= power_iterations <= 32:
+        raise ValueError("power_iterations must be in [0, 32]")
+    shape = tuple(window.encoded.codes.shape[:-2])
+    if workspace is None:
+        workspace = torch.empty((*shape, VALUE_DIMENSION, KEY_DIMENSION), dtype=torch.float32,
+                                device=device)
+    if _check(workspace, "workspace", torch.float32, (VALUE_DIMENSION, KEY_DIMENSION),
+              device) != heads:
+        raise ValueError("workspace must hold one [128, 128] fp32 block per state")
+    nxt = empty_encoded(shape, "provider", device)
+    next_ck = torch.empty((*shape, KEY_DIMENSION, COMPENSATOR_RANK), dtype=torch.float16,
+                          device=device)
+    next_cv = torch.empty((*shape, VALUE_DIMENSION, COMPENSATOR_RANK), dtype=torch.float16,
+                          device=device)
+    with torch.cuda.device(device):
+        _status("boundary refit", _native.call(
+            "statecentric_gdn_state_codec_window_boundary_launch_v1", _stream(device),
+            *_window_args(window), _ptr(nxt.codes), _ptr(nxt.smoothing), _ptr(nxt.scales),
+            _ptr(next_ck), _ptr(next_cv), _ptr(workspace), heads, power_iterations))
+    if window.compensator_keys is None and power_iterations == 0:
+        next_ck = next_cv = None  # still a quant-only boundary (zero compensators)
+    return WindowStates(nxt, next_ck, next_cv, window.record_decay, window.record_keys,
+                        window.record_corrections, window.positions)
+
+
+def dense_step(states: torch.Tensor, decay: torch.Tensor, keys: torch.Tensor,
+               reads: torch.Tensor, queries: torch.Tensor, values: torch.Tensor, *,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 GDN step in place on capsule-layout dense states
+    (fp32_gdn_step_launch_v1): S = decay S + key (x) (value - S^T read);
+    returns S^T query (fp32 [H, 128])."""
+    heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
+    device = states.device
+    if _check(decay, "decay", torch.float32, (), device) != heads:
+        raise ValueError("decay must hold one value per head")
+    _vectors(heads, device, torch.float16, {"keys": (keys, heads), "reads": (reads, heads),
+                                            "queries": (queries, heads),
+                                            "values": (values, heads)})
+    if out is None:
+        out = torch.empty((heads, VALUE_DIMENSION), dtype=torch.float32, device=device)
+    _vectors(heads, device, torch.float32, {"outputs": (out, heads)})
+    with torch.cuda.device(device):
+        _status("dense step", _native.call(
+            "statecentric_gdn_state_codec_fp32_gdn_step_launch_v1", _stream(device),
+            _ptr(states), _ptr(decay), _ptr(keys), _ptr(reads), _ptr(queries), _ptr(values),
+            _ptr(out), heads))
     return out
 
 

@@ -14,11 +14,14 @@ Mirrors the reference's src/gdn_state_codec/runtime.py:
     ``reconstruct``, ``invalidate``, ``decode_fallback_reason``,
     ``fall_back_to_native``, ``step`` and ``observe_shadow``.
 
-The windowed p=16 decode step (runtime.py:735-845) is not part of this
-backend: its library entry points are present for the loader and return 5,
-so ``step`` raises exactly as the reference does when a decode backend is
-unavailable.  ``boundary_readout`` gives the encoded projection S^T q of a
-slot's boundary straight from the int8 codes instead.
+The windowed p=16 decode (runtime.py:627-845) runs on the CUDA window
+kernels: ``step`` launches ``windowed_gdn_step_bf16_launch_v1`` (or its
+quant-only form) on the slot's boundary and records, and every 16 tokens
+``_refit_boundary`` folds the window into a new boundary with
+``window_boundary_launch_v1``.  The Ascend Cube decode / boundary runtimes
+have no counterpart, so ``decode_backend: cube`` raises as the reference does
+when that backend is unavailable.  ``boundary_readout`` gives the encoded
+projection S^T q of a slot's boundary straight from the int8 codes.
 """
 
 from __future__ import annotations
@@ -42,6 +45,7 @@ KEY_DIMENSION = 128
 VALUE_DIMENSION = 128
 COMPENSATOR_RANK = 4
 WINDOW_SIZE = 16
+POSITION_STRIDE = 8
 SHADOW_RELATIVE_RMS_LIMIT = 2.0e-2
 
 
@@ -57,14 +61,55 @@ def _logger():
 class _EncodedSlot:
     """One request slot's encoded GDN state for one layer (runtime.py:26-45):
     int8 codes in provider order [H, value, key], smoothing per key, scales
-    per value, rank-4 compensators (fp16, zero for quant_only)."""
+    per value, rank-4 compensators (fp16, zero for quant_only), the p=16
+    window records and position, the double-buffered next boundary the refit
+    writes, its fp32 workspace and the bf16 step output."""
 
     residual: torch.Tensor
     smoothing: torch.Tensor
     scales: torch.Tensor
     compensator_keys: torch.Tensor
     compensator_values: torch.Tensor
+    record_decay: torch.Tensor | None = None
+    record_keys: torch.Tensor | None = None
+    record_corrections: torch.Tensor | None = None
+    positions: torch.Tensor | None = None
+    scratch_residual: torch.Tensor | None = None
+    scratch_smoothing: torch.Tensor | None = None
+    scratch_scales: torch.Tensor | None = None
+    scratch_compensator_keys: torch.Tensor | None = None
+    scratch_compensator_values: torch.Tensor | None = None
+    residual_workspace: torch.Tensor | None = None
+    output: torch.Tensor | None = None
     steps: int = 0
+
+    def __post_init__(self) -> None:
+        # runtime.py:392-451: window buffers beside the boundary.
+        if self.record_keys is not None:
+            return
+        heads = self.residual.shape[0]
+        device = self.residual.device
+        self.record_decay = torch.ones((heads, WINDOW_SIZE), dtype=torch.float32, device=device)
+        self.record_keys = torch.zeros((heads, WINDOW_SIZE, KEY_DIMENSION), dtype=torch.float16,
+                                       device=device)
+        self.record_corrections = torch.zeros((heads, WINDOW_SIZE, VALUE_DIMENSION),
+                                              dtype=torch.float16, device=device)
+        self.positions = torch.zeros((heads, POSITION_STRIDE), dtype=torch.int32, device=device)
+        self.scratch_residual = torch.empty_like(self.residual)
+        self.scratch_smoothing = torch.empty_like(self.smoothing)
+        self.scratch_scales = torch.empty_like(self.scales)
+        self.scratch_compensator_keys = torch.empty_like(self.compensator_keys)
+        self.scratch_compensator_values = torch.empty_like(self.compensator_values)
+        self.residual_workspace = torch.empty(self.residual.shape, dtype=torch.float32,
+                                              device=device)
+        self.output = torch.empty((1, 1, heads, VALUE_DIMENSION), dtype=torch.bfloat16,
+                                  device=device)
+
+    def kernel_state_pointers(self) -> tuple[int, ...]:
+        return (self.residual.data_ptr(), self.smoothing.data_ptr(), self.scales.data_ptr(),
+                self.compensator_keys.data_ptr(), self.compensator_values.data_ptr(),
+                self.record_decay.data_ptr(), self.record_keys.data_ptr(),
+                self.record_corrections.data_ptr(), self.positions.data_ptr())
 
 
 _DEPENDENCIES = (
@@ -387,19 +432,43 @@ class GdnStateCodecRuntime:
         return slot
 
     def _refit_boundary(self, slot: _EncodedSlot) -> None:
-        """The p=16 window refit is not part of this backend (its entry point
-        returns 5); fail as the reference does on a failing refit launch."""
-        status = self._libraries.window_boundary(*([None] * 16), slot.residual.shape[0],
-                                                 self.experiment.boundary_power_iterations)
+        """Fold the slot's full window into a new boundary (runtime.py:627-733):
+        window_boundary_launch_v1 writes the scratch boundary, clears the
+        records and resets the position; the buffers then swap."""
+        stream = self._stream()
+        status = self._libraries.window_boundary(
+            stream.cuda_stream, *slot.kernel_state_pointers(), slot.scratch_residual.data_ptr(),
+            slot.scratch_smoothing.data_ptr(), slot.scratch_scales.data_ptr(),
+            slot.scratch_compensator_keys.data_ptr(), slot.scratch_compensator_values.data_ptr(),
+            slot.residual_workspace.data_ptr(), slot.residual.shape[0],
+            self.experiment.boundary_power_iterations)
         if status != 0:
             raise RuntimeError(f"GDN State Codec boundary-refit launch failed: {status}")
+        # The launch bypasses the allocator's stream tracking: keep the old
+        # boundary alive until the refit has read it.
+        for tensor in (slot.residual, slot.smoothing, slot.scales, slot.compensator_keys,
+                       slot.compensator_values, slot.residual_workspace):
+            tensor.record_stream(stream)
+        slot.residual, slot.scratch_residual = slot.scratch_residual, slot.residual
+        slot.smoothing, slot.scratch_smoothing = slot.scratch_smoothing, slot.smoothing
+        slot.scales, slot.scratch_scales = slot.scratch_scales, slot.scales
+        slot.compensator_keys, slot.scratch_compensator_keys = (slot.scratch_compensator_keys,
+                                                                slot.compensator_keys)
+        slot.compensator_values, slot.scratch_compensator_values = (
+            slot.scratch_compensator_values, slot.compensator_values)
+        slot.steps = 0
+        self.boundary_refits += 1
+        log = _logger().warning if self.experiment.mode == "shadow" else _logger().info
+        log("GDN State Codec boundary %s refits=%d shadow_max_relative_rms=%.8g", self.prefix,
+            self.boundary_refits, self.shadow_max_relative_rms)
 
     def step(self, provider_state: torch.Tensor, cache_index: int, query: torch.Tensor,
              key: torch.Tensor, value: torch.Tensor, log_decay: torch.Tensor,
              beta: torch.Tensor, query_scale: float) -> torch.Tensor:
-        """Windowed decode step (runtime.py:735-845): validates the Qwen3.5
-        input contract, then needs a decode backend, which this codec-only
-        backend does not provide."""
+        """Windowed decode step (runtime.py:750-845): refit at a full window,
+        validate the Qwen3.5 input contract once, then one bf16 step launch
+        (the quant-only kernel for quant-only boundaries without refit power
+        iterations); returns the slot's bf16 output [1, 1, H, 128]."""
         slot = self._slot(provider_state, cache_index)
         if slot.steps == WINDOW_SIZE:
             self._refit_boundary(slot)
@@ -425,7 +494,8 @@ class GdnStateCodecRuntime:
             if not all(t.is_contiguous() for t in (query, key, value, log_decay, beta)):
                 raise RuntimeError("GDN State Codec Qwen3.5 inputs must be contiguous")
             self._input_contract_validated = True
-        if self.experiment.decode_backend == "vector":
+        vector = self.experiment.decode_backend == "vector"
+        if vector:
             vector_step = self._libraries.window_step_bf16
             if (self.experiment.initializer == "quant_only"
                     and self.experiment.boundary_power_iterations == 0
@@ -433,11 +503,21 @@ class GdnStateCodecRuntime:
                 vector_step = self._libraries.window_step_bf16_quant_only
             if vector_step is None:
                 raise RuntimeError("GDN State Codec vector decode backend is unavailable")
-            raise RuntimeError("GDN State Codec decode-step launch failed: 5")
-        decode_handle = self._libraries.decode_handle(heads)
-        if decode_handle is None or self._libraries.decode_runtime_step is None:
-            raise RuntimeError("GDN State Codec Cube decode backend is unavailable")
-        raise RuntimeError("GDN State Codec decode-step launch failed: 5")
+        else:
+            decode_handle = self._libraries.decode_handle(heads)
+            if decode_handle is None or self._libraries.decode_runtime_step is None:
+                raise RuntimeError("GDN State Codec Cube decode backend is unavailable")
+        pointers = (self._stream().cuda_stream, *slot.kernel_state_pointers(),
+                    log_decay.data_ptr(), beta.data_ptr(), key.data_ptr(), query.data_ptr(),
+                    value.data_ptr(), slot.output.data_ptr())
+        if vector:
+            status = vector_step(*pointers, heads)
+        else:
+            status = self._libraries.decode_runtime_step(decode_handle, *pointers, heads)
+        if status != 0:
+            raise RuntimeError(f"GDN State Codec decode-step launch failed: {status}")
+        slot.steps += 1
+        return slot.output
 
     def observe_shadow(self, compressed: torch.Tensor, reference: torch.Tensor) -> float:
         """Relative RMS of a compressed output against the dense path, gated

@@ -386,3 +386,219 @@ def ref_restore_capsule(data: bytes, geometry: str = DEFAULT_GEOMETRY, generatio
         buffer.ctypes.data, buffer.size, geometry.encode(), generation, epoch, keys, values,
         message, 256)
     return status == 0, message.value.decode()
+
+
+# --------------------------------------------------------------------------
+# Windowed decode path (gdn_window_oracle.c): ReadWindowState / ApplyToken /
+# DenseState / QuantizeBoundary of capsule.cpp, with the device ABI's binary16
+# record and compensator storage as an option.
+
+WINDOW = 16
+QUERY_SCALE = np.float32(0.08838834764831845)  # 128 ** -0.5 as the reference's fp32 constant
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_window_ready = False
+
+
+def _window_lib() -> ctypes.CDLL:
+    global _window_ready
+    handle = lib()
+    if not _window_ready:
+        c_int, u32, f32 = ctypes.c_int, ctypes.c_uint32, ctypes.c_float
+        handle.oracle_window_read.argtypes = [
+            c_int, _i8p, _f32p, _f32p, _f32p, _f32p, u32, _f32p, _f32p, _f32p, _f32p, _f32p]
+        handle.oracle_window_step.argtypes = [
+            c_int, _i8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32p, f32,
+            _f32p, _f32p, _f32p, _f32p, c_int, _f32p]
+        handle.oracle_window_dense.argtypes = [
+            c_int, _i8p, _f32p, _f32p, _f32p, _f32p, u32, _f32p, _f32p, _f32p, _f32p]
+        handle.oracle_quantize_boundary.argtypes = [
+            _f32p, u32, c_int, c_int, _i8p, _f32p, _f32p, _f32p, _f32p]
+        handle.oracle_quantize_boundary.restype = c_int
+        handle.oracle_window_fold.argtypes = [
+            c_int, _i8p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32p, u32, c_int,
+            _i8p, _f32p, _f32p, _f32p, _f32p]
+        handle.oracle_window_fold.restype = c_int
+        handle.oracle_dense_step.argtypes = [_f32p, f32, _f32p, _f32p, _f32p, _f32p, _f32p]
+        handle.oracle_f32_to_f16.argtypes = [f32]
+        handle.oracle_f32_to_f16.restype = ctypes.c_uint16
+        handle.oracle_f32_to_bf16.argtypes = [f32]
+        handle.oracle_f32_to_bf16.restype = ctypes.c_uint16
+        _window_ready = True
+    return handle
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return int(_window_lib().oracle_f32_to_f16(float(x)))
+
+
+def f32_to_bf16_bits(x: float) -> int:
+    return int(_window_lib().oracle_f32_to_bf16(float(x)))
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_array(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even bfloat16 bits of a finite float32 array."""
+    bits = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+class WindowHead:
+    """One head's window: boundary (codes in ``layout``, smoothing, scales,
+    optional rank-4 compensators) plus up to 16 records and the position."""
+
+    def __init__(self, codes, smoothing, scales, compensator_keys=None,
+                 compensator_values=None, layout: str = "provider"):
+        self.provider = 1 if layout == "provider" else 0
+        self.codes = np.ascontiguousarray(codes, np.int8).reshape(128, 128)
+        self.c = np.ascontiguousarray(smoothing, np.float32).reshape(128)
+        self.b = np.ascontiguousarray(scales, np.float32).reshape(128)
+        self.ck = None if compensator_keys is None else np.ascontiguousarray(
+            compensator_keys, np.float32).reshape(128, RANK)
+        self.cv = None if compensator_values is None else np.ascontiguousarray(
+            compensator_values, np.float32).reshape(128, RANK)
+        self.rdecay = np.zeros(WINDOW, np.float32)
+        self.rkeys = np.zeros((WINDOW, 128), np.float32)
+        self.rcorr = np.zeros((WINDOW, 128), np.float32)
+        self.position = ctypes.c_uint32(0)
+
+    def _boundary(self):
+        return (self.provider, _ptr(self.codes, _i8p), _ptr(self.c, _f32p), _ptr(self.b, _f32p),
+                _ptr(self.ck, _f32p), _ptr(self.cv, _f32p))
+
+    def read(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(128, np.float32)
+        _window_lib().oracle_window_read(*self._boundary(), self.position.value,
+                                         _ptr(self.rdecay, _f32p), _ptr(self.rkeys, _f32p),
+                                         _ptr(self.rcorr, _f32p), _ptr(x, _f32p),
+                                         _ptr(out, _f32p))
+        return out
+
+    def step(self, decay, key, read, query, value, round_storage: bool = True) -> np.ndarray:
+        if self.position.value >= WINDOW:
+            raise ValueError("window is full")
+        arrays = [np.ascontiguousarray(a, np.float32) for a in (key, read, query, value)]
+        out = np.empty(128, np.float32)
+        _window_lib().oracle_window_step(
+            *self._boundary(), _ptr(self.rdecay, _f32p), _ptr(self.rkeys, _f32p),
+            _ptr(self.rcorr, _f32p), ctypes.byref(self.position), float(np.float32(decay)),
+            *[_ptr(a, _f32p) for a in arrays], int(round_storage), _ptr(out, _f32p))
+        return out
+
+    def dense(self) -> np.ndarray:
+        out = np.empty((128, 128), np.float32)
+        _window_lib().oracle_window_dense(*self._boundary(), self.position.value,
+                                          _ptr(self.rdecay, _f32p), _ptr(self.rkeys, _f32p),
+                                          _ptr(self.rcorr, _f32p), _ptr(out, _f32p))
+        return out
+
+    def fold(self, iterations: int, round_storage: bool = True) -> int:
+        """Refit the boundary from the window (records cleared, position 0).
+        Compensators are kept (zeros) even for ``iterations == 0``."""
+        codes = np.empty_like(self.codes)
+        c, b = np.empty_like(self.c), np.empty_like(self.b)
+        ck, cv = np.empty((128, RANK), np.float32), np.empty((128, RANK), np.float32)
+        status = _window_lib().oracle_window_fold(
+            *self._boundary(), _ptr(self.rdecay, _f32p), _ptr(self.rkeys, _f32p),
+            _ptr(self.rcorr, _f32p), ctypes.byref(self.position), iterations,
+            int(round_storage), _ptr(codes, _i8p), _ptr(c, _f32p), _ptr(b, _f32p),
+            _ptr(ck, _f32p), _ptr(cv, _f32p))
+        self.codes, self.c, self.b = codes, c, b
+        if self.ck is not None or iterations > 0:
+            self.ck, self.cv = ck, cv
+        return int(status)
+
+
+def quantize_boundary(dense: np.ndarray, iterations: int = 32, layout: str = "capsule",
+                      round_storage: bool = False) -> dict:
+    """QuantizeBoundary (capsule.cpp:130-225) of one capsule-order dense head."""
+    dense = np.ascontiguousarray(dense, np.float32)
+    out = {"codes": np.empty((128, 128), np.int8), "smoothing": np.empty(128, np.float32),
+           "scales": np.empty(128, np.float32),
+           "compensator_keys": np.empty((128, RANK), np.float32),
+           "compensator_values": np.empty((128, RANK), np.float32)}
+    status = _window_lib().oracle_quantize_boundary(
+        _ptr(dense, _f32p), iterations, 1 if layout == "provider" else 0, int(round_storage),
+        _ptr(out["codes"], _i8p), _ptr(out["smoothing"], _f32p), _ptr(out["scales"], _f32p),
+        _ptr(out["compensator_keys"], _f32p), _ptr(out["compensator_values"], _f32p))
+    out["status"] = int(status)
+    return out
+
+
+def dense_step(state: np.ndarray, decay, key, read, query, value) -> np.ndarray:
+    """fp32 GDN step in place on one capsule-order dense head; returns S_new^T query."""
+    assert state.dtype == np.float32 and state.flags["C_CONTIGUOUS"]
+    arrays = [np.ascontiguousarray(a, np.float32) for a in (key, read, query, value)]
+    out = np.empty(128, np.float32)
+    _window_lib().oracle_dense_step(_ptr(state, _f32p), float(np.float32(decay)),
+                                    *[_ptr(a, _f32p) for a in arrays], _ptr(out, _f32p))
+    return out
+
+
+def qwen_token(decay, beta_bits, key_bits, query_bits, value_bits):
+    """The Qwen3.5 decode token of one head as the window step consumes it:
+    decay (fp32, exp of the log decay), beta / key / query / value as bf16
+    bits.  Returns (decay, key, read, query, value) in fp32: key = beta * k
+    (exact), read = decay * k, query = 128^-0.5 * q, value = v."""
+    decay = np.float32(decay)
+    beta = bf16_bits_to_f32(np.array([beta_bits]))[0]
+    k = bf16_bits_to_f32(key_bits)
+    q = bf16_bits_to_f32(query_bits)
+    v = bf16_bits_to_f32(value_bits)
+    return decay, (beta * k).astype(np.float32), (decay * k).astype(np.float32), \
+        (QUERY_SCALE * q).astype(np.float32), v.astype(np.float32)
+
+
+def ref_apply_tokens(dense: np.ndarray, decay, key, read, query, value) -> dict:
+    """FromDenseBoundary + ApplyToken of the reference library per token
+    (scalar decay broadcast over the keys)."""
+    handle = ref()
+    if not hasattr(handle, "_apply_ready"):
+        u32 = ctypes.c_uint32
+        handle.ref_apply_tokens.argtypes = [
+            _f32p, u32, u32, u32, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+            ctypes.POINTER(ctypes.c_uint8), _f32p, _u32p]
+        handle.ref_apply_tokens.restype = ctypes.c_int
+        handle._apply_ready = True
+    dense = np.ascontiguousarray(dense, np.float32)
+    arrays = [np.ascontiguousarray(a, np.float32) for a in (decay, key, read, query, value)]
+    tokens = arrays[0].shape[0]
+    outputs = np.empty((tokens, 128), np.float32)
+    crossed = np.zeros(tokens, np.uint8)
+    final = np.empty((128, 128), np.float32)
+    position = ctypes.c_uint32(0)
+    status = handle.ref_apply_tokens(
+        _ptr(dense, _f32p), 128, 128, tokens, *[_ptr(a, _f32p) for a in arrays],
+        _ptr(outputs, _f32p), crossed.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+        _ptr(final, _f32p), ctypes.byref(position))
+    if status != 0:
+        raise ValueError("reference rejected the token sequence")
+    return {"outputs": outputs, "crossed": crossed.astype(bool), "dense": final,
+            "position": int(position.value)}
+
+
+def ref_window_read(head: "WindowHead", x: np.ndarray) -> np.ndarray:
+    """ReadWindowState of the reference library itself (ref_quant_shim.cpp)
+    for a capsule-layout WindowHead at its current position."""
+    handle = ref_quant()
+    if not hasattr(handle, "_window_ready"):
+        u32 = ctypes.c_uint32
+        handle.ref_window_read.argtypes = [
+            _i8p, _f32p, _f32p, _f32p, _f32p, u32, u32, u32, _f32p, _f32p, _f32p, _f32p, _f32p]
+        handle.ref_window_read.restype = ctypes.c_int
+        handle._window_ready = True
+    if head.provider:
+        raise ValueError("the reference reads capsule-layout boundaries")
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(128, np.float32)
+    status = handle.ref_window_read(
+        _ptr(head.codes, _i8p), _ptr(head.c, _f32p), _ptr(head.b, _f32p), _ptr(head.ck, _f32p),
+        _ptr(head.cv, _f32p), 128, 128, head.position.value, _ptr(head.rdecay, _f32p),
+        _ptr(head.rkeys, _f32p), _ptr(head.rcorr, _f32p), _ptr(x, _f32p), _ptr(out, _f32p))
+    if status != 0:
+        raise ValueError("reference window read rejected the input")
+    return out

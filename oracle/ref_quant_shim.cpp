@@ -15,7 +15,10 @@
 //                       (manifests/vllm-hust-extension-v0.3.json:64-70);
 //   DequantizeBoundary  capsule.cpp:229-251   rank 0 (no compensator terms);
 //   ReadWindowState     capsule.cpp:256-305   rank 0, no update records: the
-//                       encoded projection S^T x from the boundary.
+//                       encoded projection S^T x from the boundary; and, in
+//                       ref_window_read, with buffered update records and an
+//                       optional rank-4 boundary: the window read of the
+//                       decode step.
 //
 // The batch entry points split heads across std::threads; the reference
 // library has no shared mutable state.  Used by tests (to pin the C oracle
@@ -144,6 +147,54 @@ int ref_quant_only_project(const std::int8_t* codes, const float* smoothing,
     std::copy(out.begin(), out.end(), outputs + h * values);
   });
   return ok ? 0 : 1;
+}
+
+// ReadWindowState (capsule.cpp:256-304) of one capsule-layout head with
+// `records` buffered updates: record u has the scalar decay decay[u]
+// (broadcast over the keys), key keys[u][keys] and correction
+// corrections[u][values].  With compensator_keys / compensator_values
+// ([keys][4] / [values][4]) the boundary has rank 4, else rank 0.  out gets
+// S^T read.  Returns 0, or 1 on bad arguments or a reference exception.
+int ref_window_read(const std::int8_t* codes, const float* smoothing, const float* scales,
+                    const float* compensator_keys, const float* compensator_values,
+                    std::uint32_t keys, std::uint32_t values, std::uint32_t records,
+                    const float* decay, const float* record_keys,
+                    const float* record_corrections, const float* read, float* out) {
+  if (codes == nullptr || smoothing == nullptr || scales == nullptr || read == nullptr ||
+      out == nullptr || keys == 0 || values == 0 ||
+      (compensator_keys == nullptr) != (compensator_values == nullptr) ||
+      (records > 0 && (decay == nullptr || record_keys == nullptr ||
+                       record_corrections == nullptr))) {
+    return 1;
+  }
+  try {
+    const auto identity = Geometry(keys, values);
+    auto parameters = QuantOnly();
+    const std::size_t elements = static_cast<std::size_t>(keys) * values;
+    GdnStateCodecCapsule::Boundary boundary;
+    boundary.residual.assign(codes, codes + elements);
+    boundary.smoothing.assign(smoothing, smoothing + keys);
+    boundary.value_scales.assign(scales, scales + values);
+    if (compensator_keys != nullptr) {
+      parameters.compensator_rank = 4;
+      boundary.compensator_keys.assign(compensator_keys, compensator_keys + keys * 4);
+      boundary.compensator_values.assign(compensator_values, compensator_values + values * 4);
+    }
+    std::vector<GdnStateCodecCapsule::UpdateRecord> updates(records);
+    for (std::uint32_t u = 0; u < records; ++u) {
+      updates[u].decay.assign(keys, decay[u]);
+      updates[u].key.assign(record_keys + static_cast<std::size_t>(u) * keys,
+                            record_keys + static_cast<std::size_t>(u + 1) * keys);
+      updates[u].correction.assign(record_corrections + static_cast<std::size_t>(u) * values,
+                                   record_corrections + static_cast<std::size_t>(u + 1) * values);
+    }
+    const auto result = statecentric::ReadWindowState(
+        boundary, updates, std::span<const float>(read, keys), identity, parameters);
+    std::copy(result.begin(), result.end(), out);
+    return 0;
+  } catch (const std::exception&) {
+    return 1;
+  }
 }
 
 }  // extern "C"

@@ -198,3 +198,47 @@ extern "C" int ref_restore_capsule(const std::uint8_t* bytes, std::uint64_t size
     return 1;
   }
 }
+
+// FromDenseBoundary(dense) followed by `tokens` ApplyToken calls
+// (capsule.cpp:354-397) with a scalar decay per token broadcast over the
+// keys.  Token t reads decay[t], key/read/query [t][keys] and value
+// [t][values]; its output goes to outputs[t][values] and crossed[t] is 1 when
+// the token completed a window (the library refit its boundary).  The final
+// DenseState (capsule.cpp:337-352) goes to dense_out when it is not null.
+// Returns 0, or 1 when the reference rejects an input.
+extern "C" int ref_apply_tokens(const float* dense, std::uint32_t keys, std::uint32_t values,
+                                std::uint32_t tokens, const float* decay, const float* key,
+                                const float* read, const float* query, const float* value,
+                                float* outputs, std::uint8_t* crossed, float* dense_out,
+                                std::uint32_t* window_position) {
+  try {
+    const std::size_t elements = static_cast<std::size_t>(keys) * values;
+    std::vector<float> state(dense, dense + elements);
+    auto capsule = GdnStateCodecCapsule::FromDenseBoundary(
+        state, Identity(keys, values), GdnStateCodecParameters{});
+    for (std::uint32_t t = 0; t < tokens; ++t) {
+      GdnStateCodecTokenInput token;
+      token.decay.assign(keys, decay[t]);
+      token.key.assign(key + static_cast<std::size_t>(t) * keys,
+                       key + static_cast<std::size_t>(t + 1) * keys);
+      token.read.assign(read + static_cast<std::size_t>(t) * keys,
+                        read + static_cast<std::size_t>(t + 1) * keys);
+      token.query.assign(query + static_cast<std::size_t>(t) * keys,
+                         query + static_cast<std::size_t>(t + 1) * keys);
+      token.value.assign(value + static_cast<std::size_t>(t) * values,
+                         value + static_cast<std::size_t>(t + 1) * values);
+      const auto result = capsule.ApplyToken(token);
+      std::memcpy(outputs + static_cast<std::size_t>(t) * values, result.output.data(),
+                  values * sizeof(float));
+      if (crossed) crossed[t] = result.crossed_window_boundary ? 1 : 0;
+    }
+    if (dense_out) {
+      const auto reconstructed = capsule.DenseState();
+      std::memcpy(dense_out, reconstructed.data(), elements * sizeof(float));
+    }
+    if (window_position) *window_position = static_cast<std::uint32_t>(capsule.window_position());
+    return 0;
+  } catch (const std::exception&) {
+    return 1;
+  }
+}

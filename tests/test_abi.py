@@ -38,7 +38,8 @@ REFERENCE_LIBRARIES = {
         "encoded_projection_launch_v1", "provider_encoded_projection_launch_v1",
         "encoded_projection_indexed_launch_v1"],
     "libstatecentric_gdn_state_codec_windowed_gdn_step_kernel.so": [
-        "windowed_gdn_step_launch_v1"],
+        "windowed_gdn_step_launch_v1", "windowed_gdn_step_bf16_launch_v1",
+        "windowed_gdn_step_bf16_quant_only_launch_v1", "fp32_gdn_step_launch_v1"],
     "libstatecentric_gdn_state_codec_window_boundary_kernel.so": [
         "window_boundary_launch_v1"],
     "libstatecentric_gdn_state_codec_bf16_cube_matmul_kernel.so": [],
@@ -177,10 +178,44 @@ def test_status_and_support_entry_points_validate():
     assert call("division_selftest_v1", None, None, ALIGNED, ALIGNED, 1) == BAD_ARGS
 
 
-def test_windowed_decode_entry_points_report_not_implemented():
-    """Present for the plugin's loader only (runtime.py:71-115)."""
-    assert call("windowed_gdn_step_launch_v1", *([None] * 16), 1) == NOT_IMPLEMENTED
-    assert call("window_boundary_launch_v1", *([None] * 16), 1, 0) == NOT_IMPLEMENTED
+def _window(a=ALIGNED):
+    # codes, smoothing, scales, compensator keys / values, record decay /
+    # keys / corrections, positions
+    return [a] * 9
+
+
+def test_windowed_decode_entry_points_validate():
+    """The window launchers refuse what the reference's refuse (null
+    pointers, zero states, odd states for the bf16 step, more than 32 power
+    iterations) plus this backend's alignment rules."""
+    a, m, n = ALIGNED, MISALIGNED, None
+    token = [a] * 5 + [a]  # decay, beta / keys, queries..., outputs
+    step_bf16 = ["windowed_gdn_step_bf16_launch_v1",
+                 "windowed_gdn_step_bf16_quant_only_launch_v1"]
+    for name in step_bf16:
+        assert call(name, n, *_window(), *token, 0) == BAD_ARGS            # no states
+        assert call(name, n, *_window(), *token, 3) == BAD_ARGS            # odd states
+        assert call(name, n, *([n] + _window()[1:]), *token, 2) == BAD_ARGS  # no codes
+        assert call(name, n, *([a + 8] + _window()[1:]), *token, 2) == BAD_ARGS  # codes misaligned
+        assert call(name, n, *_window(), *token[:5], n, 2) == BAD_ARGS     # no outputs
+    # compensators: required by the full step, optional for quant-only, paired
+    w = _window()
+    w[3] = w[4] = n
+    assert call(step_bf16[0], n, *w, *token, 2) == BAD_ARGS
+    w = _window()
+    w[4] = n
+    assert call(step_bf16[1], n, *w, *token, 2) == BAD_ARGS
+    w = _window()
+    w[3] = a + 4  # compensators must be 8-byte aligned
+    assert call(step_bf16[0], n, *w, *token, 2) == BAD_ARGS
+    assert call("windowed_gdn_step_launch_v1", n, *_window(), *token, 0) == BAD_ARGS
+    assert call("windowed_gdn_step_launch_v1", n, *_window(), m + 1, *token[1:], 1) == BAD_ARGS
+    boundary = _window() + [a] * 6  # next codes / smoothing / scales / keys / values, workspace
+    assert call("window_boundary_launch_v1", n, *boundary, 1, 33) == BAD_ARGS
+    assert call("window_boundary_launch_v1", n, *boundary, 0, 0) == BAD_ARGS
+    assert call("window_boundary_launch_v1", n, *boundary[:-1], m, 1, 0) == BAD_ARGS
+    assert call("fp32_gdn_step_launch_v1", n, a, a, a, a, a, a, a, 0) == BAD_ARGS
+    assert call("fp32_gdn_step_launch_v1", n, n, a, a, a, a, a, a, 1) == BAD_ARGS
 
 
 def test_valid_arguments_without_a_device_report_setup_failure():
@@ -192,3 +227,4 @@ def test_valid_arguments_without_a_device_report_setup_failure():
     a = ALIGNED
     assert call("initialize_launch_v3", None, a, a, a, a, 1) == 3
     assert call("provider_dequantize_launch_v2", None, a, a, a, None, None, a, 1) == 3
+    assert call("windowed_gdn_step_bf16_launch_v1", None, *_window(), *([a] * 6), 2) == 3

@@ -1,6 +1,7 @@
 """GPU tests of the plugin runtime (gdn_state_codec.runtime) on the B200
 kernels: slot encode from a vLLM-style provider-layout state cache,
-reconstruction and boundary readout, checked against the CPU oracle."""
+reconstruction, boundary readout and a decode step, checked against the CPU
+oracle."""
 
 from __future__ import annotations
 
@@ -91,7 +92,7 @@ def test_exact_svd_slot_quantizes_the_residual_exactly(ssm_state):
     assert float(err) < 2e-2
 
 
-def test_step_reports_no_decode_backend_on_the_device(ssm_state):
+def test_step_runs_the_decode_kernel_on_the_device(ssm_state):
     rt = runtime()
     bf = torch.bfloat16
     inputs = dict(query=torch.zeros((1, 1, HEADS // 2, 128), dtype=bf, device=DEV),
@@ -100,6 +101,11 @@ def test_step_reports_no_decode_backend_on_the_device(ssm_state):
                   log_decay=torch.zeros((1, 1, HEADS), device=DEV),
                   beta=torch.zeros((1, 1, HEADS), dtype=bf, device=DEV),
                   query_scale=128 ** -0.5)
-    with pytest.raises(RuntimeError, match="vector decode backend is unavailable"):
-        rt.step(ssm_state, 0, **inputs)
-    assert 0 in rt._slots  # the slot was encoded before the decode request failed
+    out = rt.step(ssm_state, 0, **inputs)
+    torch.cuda.synchronize()
+    assert out.shape == (1, 1, HEADS, 128) and out.dtype == bf
+    # zero query and value: the output is exactly zero and one record is appended
+    assert not out.float().any()
+    slot = rt._slots[0]
+    assert slot.steps == 1 and bool((slot.positions[:, 0] == 1).all())
+    assert bool((slot.record_decay[:, 0] == 1.0).all())  # exp(0)

@@ -148,9 +148,12 @@ def test_libraries_load_from_the_library_dir():
     assert libraries.provider_smoothing is not None and libraries.provider_quantize is not None
     assert libraries.provider_dequantize is not None
     assert libraries.provider_encoded_projection is not None
-    # the windowed decode is a loader stub; the bf16 variants are absent
-    assert libraries.window_step is not None and libraries.window_step_bf16 is None
-    assert libraries.window_step(*([None] * 16), 1) == 5
+    # the windowed decode entry points, all resolved from the window libraries
+    assert libraries.window_step is not None and libraries.window_step_bf16 is not None
+    assert libraries.window_step_bf16_quant_only is not None
+    assert libraries.window_boundary is not None
+    assert libraries.window_step(*([None] * 16), 1) == 1       # null buffers are refused
+    assert libraries.window_boundary(*([None] * 16), 1, 0) == 1
 
 
 def test_missing_library_file_raises(tmp_path):
@@ -193,28 +196,33 @@ def _decode_inputs(heads=4):
                 query_scale=128 ** -0.5)
 
 
-@pytest.mark.parametrize("backend, message", [("vector", "vector decode backend is unavailable"),
-                                              ("cube", "Cube decode backend is unavailable")])
-def test_step_validates_inputs_then_reports_no_decode_backend(backend, message):
-    rt = runtime_mod.GdnStateCodecRuntime(_experiment(backend=backend), "layer")
+def test_step_validates_inputs_then_launches():
+    """The Qwen3.5 input contract is checked first, and the Cube backend has
+    no counterpart in this backend."""
+    rt = runtime_mod.GdnStateCodecRuntime(_experiment(backend="cube"), "layer")
     rt._slots[0] = _fake_slot()
-    with pytest.raises(RuntimeError, match=message):
+    with pytest.raises(RuntimeError, match="Cube decode backend is unavailable"):
         rt.step(torch.zeros(1), 0, **_decode_inputs())
-    rt2 = runtime_mod.GdnStateCodecRuntime(_experiment(backend=backend), "layer")
+    rt2 = runtime_mod.GdnStateCodecRuntime(_experiment(), "layer")
     rt2._slots[0] = _fake_slot()
     bad = _decode_inputs()
     bad["query_scale"] = 0.5
     with pytest.raises(RuntimeError, match="query scale is unsupported"):
         rt2.step(torch.zeros(1), 0, **bad)
+    bad = _decode_inputs()
+    bad["value"] = bad["value"][..., :64]
+    with pytest.raises(RuntimeError, match=r"requires \[1,1,H,128\] value"):
+        rt2.step(torch.zeros(1), 0, **bad)
 
 
-def test_step_at_window_end_reports_the_refit_status():
-    rt = runtime_mod.GdnStateCodecRuntime(_experiment(), "layer")
-    slot = _fake_slot()
-    slot.steps = runtime_mod.WINDOW_SIZE
-    rt._slots[0] = slot
-    with pytest.raises(RuntimeError, match="boundary-refit launch failed: 5"):
-        rt.step(torch.zeros(1), 0, **_decode_inputs())
+def test_slot_carries_window_buffers():
+    slot = _fake_slot(heads=6)
+    assert slot.record_keys.shape == (6, 16, 128) and slot.record_keys.dtype == torch.float16
+    assert slot.record_corrections.shape == (6, 16, 128)
+    assert slot.record_decay.shape == (6, 16) and slot.positions.shape == (6, 8)
+    assert slot.residual_workspace.shape == (6, 128, 128)
+    assert slot.output.shape == (1, 1, 6, 128) and slot.output.dtype == torch.bfloat16
+    assert len(slot.kernel_state_pointers()) == 9
 
 
 def test_slot_index_out_of_range():
