@@ -56,6 +56,9 @@ def parse_args():
                         help="request slots per GPU (default: config 2's 64)")
     parser.add_argument("--profile", action="store_true",
                         help="device-resident steps only (for ncu captures of a small case)")
+    parser.add_argument("--profile-decode", action="store_true",
+                        help="device-resident decode windows only (16 steps + refit per "
+                             "window), for ncu captures of the window kernels")
     parser.add_argument("--profile-full", action="store_true",
                         help="device-resident full-codec launches only (fit + quantize), "
                              "warm-up + steps of them, for ncu captures of the fit kernel")
@@ -233,7 +236,7 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.warmup < 3 and not (args.profile or args.profile_full):
+    if args.warmup < 3 and not (args.profile or args.profile_full or args.profile_decode):
         raise SystemExit("--warmup must be >= 3")
 
     import torch
@@ -267,6 +270,16 @@ def main() -> None:
     layout = args.layout
     states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=0,
                                      slot_base=shard.base, device=device)
+    if args.profile_decode:
+        decode_measure(codec, torch, device, barrier, max_over_ranks, slots,
+                       windows=args.warmup + args.steps, timed=False)
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile_decode": True, "heads": heads,
+                              "windows": args.warmup + args.steps}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.profile_full:
         for _ in range(args.warmup + args.steps):
             codec.full_encode(states, layout)
@@ -360,6 +373,8 @@ def main() -> None:
     box = box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
                       rank, world)
     torch.cuda.empty_cache()
+    decode = decode_measure(codec, torch, device, barrier, max_over_ranks, SLOTS)
+    torch.cuda.empty_cache()
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -401,6 +416,7 @@ def main() -> None:
             "full_codec": full,
             "config4_ragged": ragged,
             "config5_box": box,
+            "decode_window": decode,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
@@ -517,6 +533,111 @@ def box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
             "scaling": "strong", "steps": iters, "ms_per_step": ms,
             "states_per_s": 2048 * per_slot / (ms / 1e3),
             "hbm_gbs_per_gpu": per_head * heads / (ms / 1e3) / 1e9}
+
+
+# Algorithmic bytes of one decode step per head at window position p
+# (provider codes + smoothing + scales, p records read, the appended record,
+# the record decay and position, q / k shared by two heads, value, beta, log
+# decay, bf16 output).
+def decode_step_bytes(position: float) -> float:
+    return (16384 + 512 + 512 + position * (256 + 256 + 4) + (256 + 256 + 4 + 4)
+            + 256 + 256 + 2 + 4 + 256)
+
+
+def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows: int = 4,
+                   timed: bool = True):
+    """The Qwen3.5 windowed decode on `slots` x 30 layers x 32 heads per GPU
+    (provider layout, quant-only boundary, the plugin's default): each window
+    is 16 bf16 decode steps over every head then the quant-only boundary
+    refit.  Reports per-step and per-refit device time, head-steps/s and the
+    step's algorithmic GB/s; and, for comparison, the dense fp32 GDN step
+    (fp32_gdn_step_launch_v1) over the same heads."""
+    heads = slots * LAYERS * HEADS
+    states = codec.synthesize_states(slots, LAYERS, HEADS, layout="provider", seed=5,
+                                     device=device).reshape(heads, 128, 128)
+    window = codec.new_window(codec.quantize(states, "provider"))
+    gen = torch.Generator(device=device).manual_seed(9)
+    steps = 16
+    log_decay = -(0.005 + 0.095 * torch.rand((steps, heads), generator=gen, device=device))
+    beta = torch.rand((steps, heads), generator=gen, device=device).to(torch.bfloat16)
+
+    def unit(shape):
+        x = torch.randn(shape, generator=gen, device=device)
+        return (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+    keys, queries = unit((steps, heads // 2, 128)), unit((steps, heads // 2, 128))
+    values = torch.randn((steps, heads, 128), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((heads, 128), dtype=torch.bfloat16, device=device)
+    workspace = torch.empty((heads, 128, 128), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    events = []
+
+    def run_window(record):
+        nonlocal window
+        for t in range(steps):
+            if record:
+                events.append(("step", torch.cuda.Event(enable_timing=True),
+                               torch.cuda.Event(enable_timing=True)))
+                events[-1][1].record(stream)
+            codec.window_step_bf16(window, log_decay[t], beta[t], keys[t], queries[t],
+                                   values[t], out=out)
+            if record:
+                events[-1][2].record(stream)
+        if record:
+            events.append(("refit", torch.cuda.Event(enable_timing=True),
+                           torch.cuda.Event(enable_timing=True)))
+            events[-1][1].record(stream)
+        window = codec.window_refit(window, 0, workspace=workspace)
+        if record:
+            events[-1][2].record(stream)
+
+    if not timed:
+        for _ in range(windows):
+            run_window(False)
+        return None
+    run_window(False)  # warm-up window
+    barrier()
+    for _ in range(windows):
+        run_window(True)
+    barrier()
+    step_ms = [s.elapsed_time(e) for kind, s, e in events if kind == "step"]
+    refit_ms = [s.elapsed_time(e) for kind, s, e in events if kind == "refit"]
+    step = max_over_ranks(sum(step_ms) / len(step_ms))
+    refit = max_over_ranks(sum(refit_ms) / len(refit_ms))
+    mean_bytes = sum(decode_step_bytes(p) for p in range(steps)) / steps
+    by_position = [sum(step_ms[w * steps + p] for w in range(windows)) / windows
+                   for p in (0, steps - 1)]
+    del workspace, states
+    torch.cuda.empty_cache()
+    # dense fp32 GDN step over the same heads (capsule layout, in place)
+    dense = codec.synthesize_states(slots, LAYERS, HEADS, layout="capsule", seed=5,
+                                    device=device).reshape(heads, 128, 128)
+    half = torch.float16
+    decay = torch.exp(log_decay[0]).contiguous()
+    k16 = keys[0].to(half).repeat_interleave(2, dim=0).contiguous()
+    q16 = queries[0].to(half).repeat_interleave(2, dim=0).contiguous()
+    v16 = values[0].to(half).contiguous()
+    dense_out = torch.empty((heads, 128), dtype=torch.float32, device=device)
+    for _ in range(2):
+        codec.dense_step(dense, decay, k16, k16, q16, v16, out=dense_out)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        codec.dense_step(dense, decay, k16, k16, q16, v16, out=dense_out)
+    end.record(stream)
+    barrier()
+    dense_ms = max_over_ranks(start.elapsed_time(end) / steps)
+    del dense
+    return {"heads": heads, "layout": "provider", "boundary": "quant-only",
+            "windows": windows, "step_ms": step, "step_ms_at_position": {"0": by_position[0],
+                                                                      "15": by_position[1]},
+            "head_steps_per_s": heads / (step / 1e3),
+            "step_gbs": mean_bytes * heads / (step / 1e3) / 1e9,
+            "step_bytes_per_head_mean": mean_bytes, "refit_ms": refit,
+            "window_head_steps_per_s": heads * steps / ((steps * step + refit) / 1e3),
+            "dense_fp32_step_ms": dense_ms,
+            "dense_fp32_step_gbs": 2 * 65536 * heads / (dense_ms / 1e3) / 1e9}
 
 
 def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank):

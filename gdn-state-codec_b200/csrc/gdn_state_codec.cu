@@ -87,7 +87,8 @@ const DeviceSetup* device_setup() {
   if (prepare_fit(&s.fit_blocks) != cudaSuccess || s.fit_blocks < 1) return nullptr;
   if (prepare_capsule() != cudaSuccess) return nullptr;
   if (prepare_window(&s.window) != cudaSuccess || s.window.fold < 1 ||
-      s.window.dense < 1 || s.window.step[0][0] < 1 || s.window.step[0][1] < 1 ||
+      s.window.dense < 1 || s.window.window_dense < 1 || s.window.step[0][0] < 1 ||
+      s.window.step[0][1] < 1 ||
       s.window.step[1][0] < 1 || s.window.step[1][1] < 1) {
     return nullptr;
   }
@@ -608,8 +609,9 @@ namespace {
 bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
 
-// The window buffers every step / refit reads: codes 16-byte aligned (vector
-// loads), compensators (when given) 8-byte aligned, the rest naturally.
+// The window buffers every step / refit reads: all 16-byte aligned (the
+// kernels load codes, smoothing pairs, compensator rows and record-key pairs
+// as vectors).
 bool window_ok(const WindowBuffers& w, bool need_compensators) {
   if (w.codes == nullptr || w.smoothing == nullptr || w.scales == nullptr ||
       w.record_decay == nullptr || w.record_keys == nullptr || w.record_corrections == nullptr ||
@@ -618,10 +620,10 @@ bool window_ok(const WindowBuffers& w, bool need_compensators) {
   }
   if ((w.ck == nullptr) != (w.cv == nullptr)) return false;
   if (need_compensators && w.ck == nullptr) return false;
-  if (w.ck != nullptr && (!aligned8(w.ck) || !aligned8(w.cv))) return false;
-  return aligned16(w.codes) && aligned4(w.smoothing) && aligned4(w.scales) &&
-         aligned4(w.record_decay) && aligned2(w.record_keys) && aligned2(w.record_corrections) &&
-         aligned4(w.positions);
+  if (w.ck != nullptr && (!aligned16(w.ck) || !aligned16(w.cv))) return false;
+  return aligned16(w.codes) && aligned16(w.smoothing) && aligned16(w.scales) &&
+         aligned16(w.record_decay) && aligned16(w.record_keys) &&
+         aligned16(w.record_corrections) && aligned16(w.positions);
 }
 
 int32_t run_window_step(void* stream, bool qwen, bool comp, const StepParams& p) {
@@ -719,8 +721,8 @@ int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(
       next_scales == nullptr || next_compensator_keys == nullptr ||
       next_compensator_values == nullptr || residual_workspace == nullptr || states == 0u ||
       power_iterations > 32u || !aligned16(next_residual) || !aligned16(next_smoothing) ||
-      !aligned16(next_scales) || !aligned8(next_compensator_keys) ||
-      !aligned8(next_compensator_values) || !aligned16(residual_workspace)) {
+      !aligned16(next_scales) || !aligned16(next_compensator_keys) ||
+      !aligned16(next_compensator_values) || !aligned16(residual_workspace)) {
     return gdnsc::kBadArgs;
   }
   const gdnsc::DeviceSetup* s = gdnsc::device_setup();
@@ -728,10 +730,14 @@ int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const gdnsc::FoldParams fp{w, next_compensator_keys, next_compensator_values,
                              residual_workspace, states, static_cast<int>(power_iterations)};
-  if (gdnsc::launch_window_fold(fp, gdnsc::grid_for(states, s->sms, s->window.fold), st) !=
-      cudaSuccess) {
-    return gdnsc::kLaunchFailed;
-  }
+  // The quant-only refit streams the window's dense state; with power
+  // iterations the fit kernel folds and fits each head in shared memory.
+  const cudaError_t err =
+      power_iterations == 0u
+          ? gdnsc::launch_window_dense(fp, gdnsc::grid_for(states, s->sms, s->window.window_dense),
+                                       st)
+          : gdnsc::launch_window_fold(fp, gdnsc::grid_for(states, s->sms, s->window.fold), st);
+  if (err != cudaSuccess) return gdnsc::kLaunchFailed;
   return gdnsc::run_quantize(stream, true, gdnsc::kFused, residual_workspace, nullptr,
                              next_smoothing, next_residual, next_scales, states,
                              SlotMap{nullptr, 1, 1}, nullptr);

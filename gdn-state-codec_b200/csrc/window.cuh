@@ -29,9 +29,9 @@
 //
 // Design: one 128-thread CTA per head, persistent over heads.  Thread t owns
 // key t for the vector work and value column t for the readout.  The suffix-
-// decayed read vectors live in shared memory (rows padded to 129 floats so
-// the per-record projections, one thread per (record, read), are conflict-
-// free); those projections and the compensator / update projections run on
+// decayed read vectors live in shared memory (rows padded to 132 floats so
+// the per-record projections, one thread per (record, read), read four keys
+// per conflict-free vector load); those projections and the compensator / update projections run on
 // the first warps while every thread sums its column's boundary readout for
 // both reads at once with packed fp32x2 arithmetic.
 #pragma once
@@ -74,9 +74,11 @@ struct StepParams {
   uint64_t heads;
 };
 
+constexpr int kRowPad = kKeys + 4;  // 16-byte rows; 8 rows at one key hit 32 banks
+
 struct __align__(16) StepShared {
-  float suffix[2][kWindow][kKeys + 1];  // suffix-decayed read / query before record p-1-j
-  float rkey[kWindow][kKeys + 1];       // record keys (fp32)
+  float suffix[2][kWindow][kRowPad];    // suffix-decayed read / query before record p-1-j
+  float rkey[kWindow][kRowPad];         // record keys (fp32)
   float2 sfinal[kKeys];                 // (read, query) suffix after every record
   float4 ck[kKeys];                     // compensator keys
   float c[kKeys];                       // smoothing
@@ -84,6 +86,7 @@ struct __align__(16) StepShared {
   float query[kKeys];                   // query of this token (undecayed)
   float proj[2][kWindow];               // record projections per read
   float cproj[2][kRank];                // compensator projections per read
+  float rdecay[kWindow];                // record decays
   float up;                             // key . query
 };
 
@@ -110,18 +113,32 @@ __device__ __forceinline__ float chain_dot(const float* a, int sa, const float* 
   return acc;
 }
 
+// The same for two contiguous, 16-byte aligned vectors, four keys per load.
+__device__ __forceinline__ float chain_dot4(const float* a, const float* b) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float acc = 0.0F;
+#pragma unroll 8
+  for (int k4 = 0; k4 < kKeys / 4; ++k4) {
+    const float4 x = a4[k4], y = b4[k4];
+    acc = __fadd_rn(acc, __fmul_rn(x.x, y.x));
+    acc = __fadd_rn(acc, __fmul_rn(x.y, y.y));
+    acc = __fadd_rn(acc, __fmul_rn(x.z, y.z));
+    acc = __fadd_rn(acc, __fmul_rn(x.w, y.w));
+  }
+  return acc;
+}
+
 template <bool kQwen, bool kComp>
-__global__ void __launch_bounds__(kWinThreads) window_step_kernel(StepParams p) {
+__global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StepShared& sh = *reinterpret_cast<StepShared*>(smem_raw);
   const int t = threadIdx.x;
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    // Every load that does not depend on the window position is issued
+    // before the position is first used, so their latencies overlap.
     const uint32_t pos = __ldcg(p.w.positions + head * kPositionStride);
-    if (pos >= kWindow) {  // block-uniform: every thread read the same word
-      if (t == 0) report(nullptr, kStatusWindowFull);
-      continue;
-    }
-    const int np = static_cast<int>(pos);
+    const uint64_t rbase = head * kWindow;
     // ---- codes of column t (provider: one 128-byte row per value) ---------
     uint4 zrow[8];
     if constexpr (kQwen) {
@@ -169,8 +186,13 @@ __global__ void __launch_bounds__(kWinThreads) window_step_kernel(StepParams p) 
       cv_t[2] = half_to_float(vw.y & 0xFFFFu);
       cv_t[3] = half_to_float(vw.y >> 16);
     }
+    if (t < kWindow) sh.rdecay[t] = __ldcg(p.w.record_decay + rbase + t);
+    if (pos >= kWindow) {  // block-uniform: every thread read the same word
+      if (t == 0) report(nullptr, kStatusWindowFull);
+      continue;
+    }
+    const int np = static_cast<int>(pos);
     // ---- records: keys to shared memory, corrections of column t ----------
-    const uint64_t rbase = head * kWindow;
     float rc[kWindow];
 #pragma unroll
     for (int u = 0; u < kWindow; ++u) {
@@ -180,13 +202,14 @@ __global__ void __launch_bounds__(kWinThreads) window_step_kernel(StepParams p) 
         rc[u] = half_to_float(__ldcg(p.w.record_corrections + (rbase + u) * kValues + t));
       }
     }
+    __syncthreads();  // record decays in shared memory
     // ---- suffix-decayed read and query (thread t = key t) -----------------
     {
       float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
       for (int j = 0; j < np; ++j) {  // record np-1-j is read with suffix j
         sh.suffix[0][j][t] = s0;
         sh.suffix[1][j][t] = s1;
-        const float d = __ldcg(p.w.record_decay + rbase + (np - 1 - j));
+        const float d = sh.rdecay[np - 1 - j];
         s0 = __fmul_rn(s0, d);
         s1 = __fmul_rn(s1, d);
       }
@@ -195,31 +218,23 @@ __global__ void __launch_bounds__(kWinThreads) window_step_kernel(StepParams p) 
     __syncthreads();
     // ---- sequential projections: records, compensators, update -----------
     const int chains = 2 * np + (kComp ? 2 * kRank : 0) + 1;
-    if (t < chains) {
-      const float* a;
-      const float* b;
-      int sa = 1, sb = 1;
-      float* dst;
+    if (kComp && t >= 2 * np && t < 2 * np + 2 * kRank) {
+      const int i = t - 2 * np;
+      const int r = i / kRank, m = i % kRank;
+      sh.cproj[r][m] = chain_dot(reinterpret_cast<const float*>(sh.ck) + m, 4,
+                                 reinterpret_cast<const float*>(sh.sfinal) + r, 2);
+    } else if (t < chains) {
+      const float* a = sh.key;
+      const float* b = sh.query;
+      float* dst = &sh.up;
       if (t < 2 * np) {
         const int r = t / np == 0 ? 0 : 1;
         const int u = t - r * np;
         a = &sh.rkey[u][0];
         b = &sh.suffix[r][np - 1 - u][0];
         dst = &sh.proj[r][u];
-      } else if (kComp && t < 2 * np + 2 * kRank) {
-        const int i = t - 2 * np;
-        const int r = i / kRank, m = i % kRank;
-        a = reinterpret_cast<const float*>(sh.ck) + m;
-        sa = 4;
-        b = reinterpret_cast<const float*>(sh.sfinal) + r;
-        sb = 2;
-        dst = &sh.cproj[r][m];
-      } else {
-        a = sh.key;
-        b = sh.query;
-        dst = &sh.up;
       }
-      *dst = chain_dot(a, sa, b, sb);
+      *dst = chain_dot4(a, b);
     }
     // ---- boundary readout of column t for both reads ----------------------
     f2 acc = pack2(0.0F, 0.0F);
@@ -393,6 +408,128 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
   }
 }
 
+// Quant-only refit (no power iterations): the window's DenseState streamed
+// straight to the workspace, one 256-thread CTA per head.  Thread t owns key
+// t mod 128 of every other pair of value rows (rows v, v + 1 with
+// v = 2 (t / 128) + 4 i), so each element pair of a thread shares its key's
+// record keys (held in registers as broadcast pairs) and reads the two rows'
+// record corrections as one adjacent pair from shared memory.  Every element
+// follows the reference order (dequantize, compensators by rank, records
+// oldest first) in packed fp32x2 arithmetic, each product rounded before its
+// add; a row's codes and its workspace row are read and written by 128
+// consecutive threads.
+constexpr int kDenseThreads = 256;
+
+struct __align__(16) WindowDenseShared {
+  float rc[kWindow][kValues];   // record corrections
+  float cv[kRank][kValues];     // compensator values, transposed
+  float b[kValues];             // scales
+  f2 dd[kWindow];               // (decay, decay) per record
+};
+
+// a / 127 for both lanes, exact for every float (the two-term reciprocal
+// below 2^-112 is replaced by the IEEE division, as in div127_any).
+__device__ __forceinline__ f2 div127x2_any(f2 a) {
+  const float lo = lo2(a), hi = hi2(a);
+  const bool ok = (fabsf(lo) >= kDiv127Safe || lo == 0.0F) &&
+                  (fabsf(hi) >= kDiv127Safe || hi == 0.0F);
+  return ok ? div127x2(a) : pack2(div127_any(lo), div127_any(hi));
+}
+
+__global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldParams p) {
+  __shared__ WindowDenseShared sh;
+  const int t = threadIdx.x;
+  const int k = t & (kKeys - 1);
+  const int group = t >> 7;
+  const bool comp = p.w.ck != nullptr;
+  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
+    const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
+    const uint64_t rbase = head * kWindow;
+    // ---- gather: records, scales, compensators ------------------------------
+    // Records past the position are identity records (decay 1, zero key and
+    // correction): v -> RN(1 v) + RN(0 0) = v, except that a -0 may become +0,
+    // which the INT8 stage maps to the same codes, smoothing and scales.  The
+    // record loop below is then free of position tests.
+    for (int i = t; i < kWindow * kValues; i += kDenseThreads) {
+      (&sh.rc[0][0])[i] = i < np * kValues
+                              ? half_to_float(__ldcg(p.w.record_corrections + rbase * kValues + i))
+                              : 0.0F;
+    }
+    if (t < kValues) {
+      sh.b[t] = __ldg(p.w.scales + head * kValues + t);
+      if (comp) {
+        const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
+        sh.cv[0][t] = half_to_float(vw.x & 0xFFFFu);
+        sh.cv[1][t] = half_to_float(vw.x >> 16);
+        sh.cv[2][t] = half_to_float(vw.y & 0xFFFFu);
+        sh.cv[3][t] = half_to_float(vw.y >> 16);
+      }
+    }
+    if (t < kWindow) {
+      const float d = t < np ? __ldcg(p.w.record_decay + rbase + t) : 1.0F;
+      sh.dd[t] = pack2(d, d);
+    }
+    f2 rk[kWindow];
+#pragma unroll
+    for (int u = 0; u < kWindow; ++u) {
+      float r = 0.0F;
+      if (u < np) r = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + k));
+      rk[u] = pack2(r, r);
+    }
+    f2 ck[kRank] = {0ull, 0ull, 0ull, 0ull};
+    if (comp) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2*>(p.w.ck + (head * kKeys + k) * kRank));
+      const float c0 = half_to_float(w.x & 0xFFFFu), c1 = half_to_float(w.x >> 16);
+      const float c2 = half_to_float(w.y & 0xFFFFu), c3 = half_to_float(w.y >> 16);
+      ck[0] = pack2(c0, c0);
+      ck[1] = pack2(c1, c1);
+      ck[2] = pack2(c2, c2);
+      ck[3] = pack2(c3, c3);
+    }
+    const float ct = __ldg(p.w.smoothing + head * kKeys + k);
+    const f2 cc = pack2(ct, ct);
+    __syncthreads();
+    // ---- the window is about to be folded: clear it --------------------------
+    for (int i = t; i < kWindow * kKeys; i += kDenseThreads) {
+      p.w.record_keys[rbase * kKeys + i] = 0;
+      p.w.record_corrections[rbase * kValues + i] = 0;
+    }
+    if (t < kWindow) p.w.record_decay[rbase + t] = 0.0F;
+    if (t == 0) p.w.positions[head * kPositionStride] = 0u;
+    if (t < kKeys) {
+      reinterpret_cast<uint2*>(p.next_ck + (head * kKeys + t) * kRank)[0] = make_uint2(0u, 0u);
+      reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
+    }
+    // ---- dense rows, two at a time -------------------------------------------
+    const int8_t* codes = p.w.codes + head * kElements + k;  // provider [v][k]
+    float* out = p.workspace + head * kElements + k;
+    bool finite = true;
+#pragma unroll 2
+    for (int i = 0; i < kValues / 4; ++i) {
+      const int v = 2 * group + 4 * i;
+      const f2 z = pack2(static_cast<float>(__ldcs(codes + v * kKeys)),
+                         static_cast<float>(__ldcs(codes + (v + 1) * kKeys)));
+      f2 val = mul2(div127x2_any(mul2(cc, z)), *reinterpret_cast<const f2*>(&sh.b[v]));
+      if (comp) {
+#pragma unroll
+        for (int m = 0; m < kRank; ++m) {
+          val = add2(val, mul2_for_add(ck[m], *reinterpret_cast<const f2*>(&sh.cv[m][v])));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kWindow; ++u) {
+        val = add2(mul2_for_add(sh.dd[u], val),
+                   mul2_for_add(rk[u], *reinterpret_cast<const f2*>(&sh.rc[u][v])));
+      }
+      finite = finite && isfinite(lo2(val)) && isfinite(hi2(val));
+      __stcg(out + v * kKeys, lo2(val));
+      __stcg(out + (v + 1) * kKeys, hi2(val));
+    }
+    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
+  }
+}
+
 inline size_t window_fold_smem_bytes() {
   return ((sizeof(FitShared) + 15) & ~size_t{15}) + sizeof(FoldExtra);
 }
@@ -448,6 +585,7 @@ __global__ void __launch_bounds__(kWinThreads) dense_step_kernel(DenseStepParams
 struct WindowBlocks {
   int step[2][2] = {};  // [qwen][comp] blocks per SM
   int fold = 0;
+  int window_dense = 0;
   int dense = 0;
 };
 
@@ -472,6 +610,9 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   if (err != cudaSuccess) return err;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->fold, window_fold_kernel, kFitThreads,
                                                       window_fold_smem_bytes());
+  if (err != cudaSuccess) return err;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense, window_dense_kernel,
+                                                      kDenseThreads, 0);
   if (err != cudaSuccess) return err;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->dense, dense_step_kernel, kWinThreads, 0);
 }
@@ -499,6 +640,11 @@ inline cudaError_t launch_window_fold(const FoldParams& p, int grid, cudaStream_
   cfg.dynamicSmemBytes = window_fold_smem_bytes();
   cfg.stream = stream;
   return cudaLaunchKernelEx(&cfg, window_fold_kernel, p);
+}
+
+inline cudaError_t launch_window_dense(const FoldParams& p, int grid, cudaStream_t stream) {
+  window_dense_kernel<<<grid, kDenseThreads, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 inline cudaError_t launch_dense_step(const DenseStepParams& p, int grid, cudaStream_t stream) {

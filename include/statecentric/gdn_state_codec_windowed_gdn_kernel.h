@@ -34,9 +34,9 @@
  * Common rules: stream is a cudaStream_t (NULL: default stream); every
  * pointer is a device pointer owned by the caller; launches are
  * asynchronous; nothing is allocated.  Return 0 enqueued, 1 bad arguments
- * (a null required pointer, states == 0, misalignment: codes 16 bytes,
- * compensators 8 bytes, others natural), 2 launch failed, 3 device set-up
- * failed.  `states` may be any value >= 1 (the Ascend launchers capped it at
+ * (a null required pointer, states == 0, a window or boundary buffer not
+ * 16-byte aligned, a token vector not naturally aligned), 2 launch failed,
+ * 3 device set-up failed.  `states` may be any value >= 1 (the Ascend launchers capped it at
  * 16384).  A step on a head whose window is already full (position 16)
  * leaves that head untouched and sets bit 8 of the sticky device error word
  * (statecentric_gdn_state_codec_device_error_v1); a non-finite output sets
@@ -101,9 +101,8 @@ int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
 /* Boundary refit (reference header :48-60): folds each head's window (its
  * `position` records, normally 16) into a new INT8 boundary plus binary16
  * compensators in the next_* buffers, then clears the records (decay, keys
- * and corrections zero) and sets the position to 0.  Codes [value][key]
- * (16-byte aligned), residual_workspace [states][128][128] fp32 (16-byte
- * aligned), power_iterations <= 32.  Input and output boundary buffers must
+ * and corrections zero) and sets the position to 0.  Codes [value][key],
+ * residual_workspace [states][128][128] fp32, power_iterations <= 32.  Input and output boundary buffers must
  * not alias.  Compensators of the current boundary may be NULL (quant-only
  * boundary). */
 int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(

@@ -206,7 +206,7 @@ def test_windowed_decode_entry_points_validate():
     w[4] = n
     assert call(step_bf16[1], n, *w, *token, 2) == BAD_ARGS
     w = _window()
-    w[3] = a + 4  # compensators must be 8-byte aligned
+    w[3] = a + 8  # compensators must be 16-byte aligned
     assert call(step_bf16[0], n, *w, *token, 2) == BAD_ARGS
     assert call("windowed_gdn_step_launch_v1", n, *_window(), *token, 0) == BAD_ARGS
     assert call("windowed_gdn_step_launch_v1", n, *_window(), m + 1, *token[1:], 1) == BAD_ARGS

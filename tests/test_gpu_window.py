@@ -228,3 +228,20 @@ def test_runtime_decode_matches_oracle():
         got = out.reshape(nheads, 128).view(torch.int16).cpu().numpy().view(np.uint16)
         assert np.array_equal(got, oracle.f32_to_bf16_array(np.stack(want))), f"token {t}"
     assert rt.boundary_refits == 1
+
+
+@pytest.mark.parametrize("compensators, iterations", [(False, 0), (True, 0), (True, 8)])
+def test_refit_of_a_partial_window_matches_oracle(compensators, iterations):
+    """A refit at position 7 (the probe case): the folded boundary and the
+    cleared window, bit-identical to the oracle."""
+    case = wc.step_probe_case(states=8, position=7)
+    window = window_from_case(case, "provider", compensators)
+    heads = wc.window_heads(case, "provider", compensators)
+    nxt = codec.window_refit(window, iterations)
+    for h in heads:
+        assert h.fold(iterations, round_storage=True) == 0
+        if not compensators and iterations == 0:
+            h.ck = h.cv = None
+    _assert_boundary(nxt, heads, f"partial refit ({iterations})")
+    check_records(nxt, heads, "partial refit")
+    assert (nxt.compensator_keys is None) == (not compensators and iterations == 0)
