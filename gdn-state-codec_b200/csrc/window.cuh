@@ -31,9 +31,10 @@
 // key t for the vector work and value column t for the readout.  The suffix-
 // decayed read vectors live in shared memory (rows padded to 132 floats so
 // the per-record projections, one thread per (record, read), read four keys
-// per conflict-free vector load); those projections and the compensator / update projections run on
-// the first warps while every thread sums its column's boundary readout for
-// both reads at once with packed fp32x2 arithmetic.
+// per conflict-free vector load); those projections and the compensator /
+// update projections run on the first warps while every thread sums its
+// column's boundary readout for both reads at once, two consecutive keys per
+// packed fp32x2 product.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -79,7 +80,8 @@ constexpr int kRowPad = kKeys + 4;  // 16-byte rows; 8 rows at one key hit 32 ba
 struct __align__(16) StepShared {
   float suffix[2][kWindow][kRowPad];    // suffix-decayed read / query before record p-1-j
   float rkey[kWindow][kRowPad];         // record keys (fp32)
-  float2 sfinal[kKeys];                 // (read, query) suffix after every record
+  float4 sq[kKeys / 2];                  // suffix after every record, per key pair j:
+                                        // (read 2j, read 2j+1, query 2j, query 2j+1)
   float4 ck[kKeys];                     // compensator keys
   float c[kKeys];                       // smoothing
   float key[kKeys];                     // write key of this token
@@ -187,22 +189,21 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
       cv_t[3] = half_to_float(vw.y >> 16);
     }
     if (t < kWindow) sh.rdecay[t] = __ldcg(p.w.record_decay + rbase + t);
+    // ---- records: keys to shared memory, corrections of column t ----------
+    // All 16 slots are read before the position is known, so a head costs one
+    // memory round trip; slots at or past the position are never used.
+    float rc[kWindow];
+#pragma unroll
+    for (int u = 0; u < kWindow; ++u) {
+      sh.rkey[u][t] = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + t));
+      rc[u] = half_to_float(__ldcg(p.w.record_corrections + (rbase + u) * kValues + t));
+    }
     if (pos >= kWindow) {  // block-uniform: every thread read the same word
       if (t == 0) report(nullptr, kStatusWindowFull);
       continue;
     }
     const int np = static_cast<int>(pos);
-    // ---- records: keys to shared memory, corrections of column t ----------
-    float rc[kWindow];
-#pragma unroll
-    for (int u = 0; u < kWindow; ++u) {
-      rc[u] = 0.0F;
-      if (u < np) {
-        sh.rkey[u][t] = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + t));
-        rc[u] = half_to_float(__ldcg(p.w.record_corrections + (rbase + u) * kValues + t));
-      }
-    }
-    __syncthreads();  // record decays in shared memory
+    __syncthreads();  // record keys and decays in shared memory
     // ---- suffix-decayed read and query (thread t = key t) -----------------
     {
       float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
@@ -213,7 +214,9 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
         s0 = __fmul_rn(s0, d);
         s1 = __fmul_rn(s1, d);
       }
-      sh.sfinal[t] = make_float2(s0, s1);
+      float* sq = reinterpret_cast<float*>(sh.sq) + 4 * (t >> 1) + (t & 1);
+      sq[0] = s0;
+      sq[2] = s1;
     }
     __syncthreads();
     // ---- sequential projections: records, compensators, update -----------
@@ -221,8 +224,14 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
     if (kComp && t >= 2 * np && t < 2 * np + 2 * kRank) {
       const int i = t - 2 * np;
       const int r = i / kRank, m = i % kRank;
-      sh.cproj[r][m] = chain_dot(reinterpret_cast<const float*>(sh.ck) + m, 4,
-                                 reinterpret_cast<const float*>(sh.sfinal) + r, 2);
+      const float* ck = reinterpret_cast<const float*>(sh.ck) + m;
+      const float* sq = reinterpret_cast<const float*>(sh.sq) + 2 * r;
+      float acc = 0.0F;
+#pragma unroll 8
+      for (int k = 0; k < kKeys; ++k) {
+        acc = __fadd_rn(acc, __fmul_rn(ck[4 * k], sq[4 * (k >> 1) + (k & 1)]));
+      }
+      sh.cproj[r][m] = acc;
     } else if (t < chains) {
       const float* a = sh.key;
       const float* b = sh.query;
@@ -237,8 +246,9 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
       *dst = chain_dot4(a, b);
     }
     // ---- boundary readout of column t for both reads ----------------------
-    f2 acc = pack2(0.0F, 0.0F);
-    const f2* sf = reinterpret_cast<const f2*>(sh.sfinal);
+    // Products of two consecutive keys are formed as one packed pair per
+    // read; the sums take them in key order.
+    float acc0 = 0.0F, acc1 = 0.0F;
     if constexpr (kQwen) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -248,20 +258,29 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
           const int k0 = 16 * i + 4 * w;
           f2 z01, z23;
           unpack_codes(words[w], z01, z23);
-          const f2 zc01 = mul2(z01, *reinterpret_cast<const f2*>(&sh.c[k0]));
-          const f2 zc23 = mul2(z23, *reinterpret_cast<const f2*>(&sh.c[k0 + 2]));
-          acc = add2(acc, mul2_for_add(pack2(lo2(zc01), lo2(zc01)), sf[k0]));
-          acc = add2(acc, mul2_for_add(pack2(hi2(zc01), hi2(zc01)), sf[k0 + 1]));
-          acc = add2(acc, mul2_for_add(pack2(lo2(zc23), lo2(zc23)), sf[k0 + 2]));
-          acc = add2(acc, mul2_for_add(pack2(hi2(zc23), hi2(zc23)), sf[k0 + 3]));
+          const float4 c4 = *reinterpret_cast<const float4*>(&sh.c[k0]);
+          const f2 zc01 = mul2(z01, pack2(c4.x, c4.y));
+          const f2 zc23 = mul2(z23, pack2(c4.z, c4.w));
+          const float4 sa = sh.sq[k0 >> 1], sb = sh.sq[(k0 >> 1) + 1];
+          f2 p0 = mul2_for_add(zc01, pack2(sa.x, sa.y));
+          f2 p1 = mul2_for_add(zc01, pack2(sa.z, sa.w));
+          acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+          acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
+          p0 = mul2_for_add(zc23, pack2(sb.x, sb.y));
+          p1 = mul2_for_add(zc23, pack2(sb.z, sb.w));
+          acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+          acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
         }
       }
     } else {
       const int8_t* staged = reinterpret_cast<StepSharedCapsule*>(smem_raw)->codes;
+      const float* sq = reinterpret_cast<const float*>(sh.sq);
 #pragma unroll 8
       for (int k = 0; k < kKeys; ++k) {
         const float zc = __fmul_rn(static_cast<float>(staged[k * kValues + t]), sh.c[k]);
-        acc = add2(acc, mul2_for_add(pack2(zc, zc), sf[k]));
+        const int j = 4 * (k >> 1) + (k & 1);
+        acc0 = __fadd_rn(acc0, __fmul_rn(zc, sq[j]));
+        acc1 = __fadd_rn(acc1, __fmul_rn(zc, sq[j + 2]));
       }
     }
     __syncthreads();
@@ -274,8 +293,8 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
         out1 = __fadd_rn(out1, __fmul_rn(rc[u], sh.proj[1][u]));
       }
     }
-    out0 = __fadd_rn(out0, __fmul_rn(div127_any(lo2(acc)), b_t));
-    out1 = __fadd_rn(out1, __fmul_rn(div127_any(hi2(acc)), b_t));
+    out0 = __fadd_rn(out0, __fmul_rn(div127_any(acc0), b_t));
+    out1 = __fadd_rn(out1, __fmul_rn(div127_any(acc1), b_t));
     if constexpr (kComp) {
 #pragma unroll
       for (int m = 0; m < kRank; ++m) {
@@ -421,6 +440,7 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
 constexpr int kDenseThreads = 256;
 
 struct __align__(16) WindowDenseShared {
+  int8_t codes[kElements];      // the head's codes, provider [v][k]
   float rc[kWindow][kValues];   // record corrections
   float cv[kRank][kValues];     // compensator values, transposed
   float b[kValues];             // scales
@@ -446,7 +466,14 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
     const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
     const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
     const uint64_t rbase = head * kWindow;
-    // ---- gather: records, scales, compensators ------------------------------
+    // ---- gather: codes, records, scales, compensators ------------------------
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(p.w.codes + head * kElements);
+#pragma unroll
+      for (int i = 0; i < kElements / 16 / kDenseThreads; ++i) {
+        reinterpret_cast<uint4*>(sh.codes)[t + kDenseThreads * i] = __ldcs(src + t + kDenseThreads * i);
+      }
+    }
     // Records past the position are identity records (decay 1, zero key and
     // correction): v -> RN(1 v) + RN(0 0) = v, except that a -0 may become +0,
     // which the INT8 stage maps to the same codes, smoothing and scales.  The
@@ -502,14 +529,14 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
       reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
     }
     // ---- dense rows, two at a time -------------------------------------------
-    const int8_t* codes = p.w.codes + head * kElements + k;  // provider [v][k]
+    const int8_t* codes = sh.codes + k;  // provider [v][k]
     float* out = p.workspace + head * kElements + k;
     bool finite = true;
 #pragma unroll 2
     for (int i = 0; i < kValues / 4; ++i) {
       const int v = 2 * group + 4 * i;
-      const f2 z = pack2(static_cast<float>(__ldcs(codes + v * kKeys)),
-                         static_cast<float>(__ldcs(codes + (v + 1) * kKeys)));
+      const f2 z = pack2(static_cast<float>(codes[v * kKeys]),
+                         static_cast<float>(codes[(v + 1) * kKeys]));
       f2 val = mul2(div127x2_any(mul2(cc, z)), *reinterpret_cast<const f2*>(&sh.b[v]));
       if (comp) {
 #pragma unroll
