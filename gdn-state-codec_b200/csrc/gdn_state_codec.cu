@@ -35,7 +35,6 @@ constexpr int32_t kOk = 0;
 constexpr int32_t kBadArgs = 1;
 constexpr int32_t kLaunchFailed = 2;
 constexpr int32_t kSetupFailed = 3;
-constexpr int32_t kNotImplemented = 5;
 constexpr int kMaxDevices = 64;
 
 struct DeviceSetup {

@@ -207,12 +207,15 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
     // ---- suffix-decayed read and query (thread t = key t) -----------------
     {
       float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
-      for (int j = 0; j < np; ++j) {  // record np-1-j is read with suffix j
-        sh.suffix[0][j][t] = s0;
-        sh.suffix[1][j][t] = s1;
-        const float d = sh.rdecay[np - 1 - j];
-        s0 = __fmul_rn(s0, d);
-        s1 = __fmul_rn(s1, d);
+#pragma unroll
+      for (int u = kWindow - 1; u >= 0; --u) {  // record u is read with suffix np-1-u
+        if (u < np) {
+          sh.suffix[0][np - 1 - u][t] = s0;
+          sh.suffix[1][np - 1 - u][t] = s1;
+          const float d = sh.rdecay[u];
+          s0 = __fmul_rn(s0, d);
+          s1 = __fmul_rn(s1, d);
+        }
       }
       float* sq = reinterpret_cast<float*>(sh.sq) + 4 * (t >> 1) + (t & 1);
       sq[0] = s0;
