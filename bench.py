@@ -359,7 +359,7 @@ def main() -> None:
     proj_ms = max_over_ranks(p_start.elapsed_time(p_end)) / proj_iters
 
     # ---- full codec (rank-4 fit + int8 stage) on a smaller batch --------------
-    full = full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank)
+    full = full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank, world)
 
     # ---- end to end through the public API with host buffers -----------------
     e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
@@ -373,7 +373,7 @@ def main() -> None:
     box = box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
                       rank, world)
     torch.cuda.empty_cache()
-    decode = decode_measure(codec, torch, device, barrier, max_over_ranks, SLOTS)
+    decode = decode_measure(codec, torch, device, barrier, max_over_ranks, SLOTS, world=world)
     torch.cuda.empty_cache()
 
     if rank == 0:
@@ -545,13 +545,14 @@ def decode_step_bytes(position: float) -> float:
 
 
 def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows: int = 4,
-                   timed: bool = True):
+                   timed: bool = True, world: int = 1):
     """The Qwen3.5 windowed decode on `slots` x 30 layers x 32 heads per GPU
     (provider layout, quant-only boundary, the plugin's default): each window
     is 16 bf16 decode steps over every head then the quant-only boundary
     refit.  Reports per-step and per-refit device time, head-steps/s and the
     step's algorithmic GB/s; and, for comparison, the dense fp32 GDN step
-    (fp32_gdn_step_launch_v1) over the same heads."""
+    (fp32_gdn_step_launch_v1) over the same heads.  Rates are whole-job
+    (every rank runs its own `slots`; times are the max over ranks)."""
     heads = slots * LAYERS * HEADS
     states = codec.synthesize_states(slots, LAYERS, HEADS, layout="provider", seed=5,
                                      device=device).reshape(heads, 128, 128)
@@ -629,21 +630,21 @@ def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows
     barrier()
     dense_ms = max_over_ranks(start.elapsed_time(end) / steps)
     del dense
-    return {"heads": heads, "layout": "provider", "boundary": "quant-only",
+    return {"heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
             "windows": windows, "step_ms": step, "step_ms_at_position": {"0": by_position[0],
                                                                       "15": by_position[1]},
-            "head_steps_per_s": heads / (step / 1e3),
-            "step_gbs": mean_bytes * heads / (step / 1e3) / 1e9,
+            "head_steps_per_s": world * heads / (step / 1e3),
+            "step_gbs_per_gpu": mean_bytes * heads / (step / 1e3) / 1e9,
             "step_bytes_per_head_mean": mean_bytes, "refit_ms": refit,
-            "window_head_steps_per_s": heads * steps / ((steps * step + refit) / 1e3),
+            "window_head_steps_per_s": world * heads * steps / ((steps * step + refit) / 1e3),
             "dense_fp32_step_ms": dense_ms,
-            "dense_fp32_step_gbs": 2 * 65536 * heads / (dense_ms / 1e3) / 1e9}
+            "dense_fp32_step_gbs_per_gpu": 2 * 65536 * heads / (dense_ms / 1e3) / 1e9}
 
 
-def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank):
+def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank, world=1):
     """The reference's full encode (FromDenseBoundary: rank-4 fit + int8 stage)
-    on 8 slots x 30 layers x 32 heads per GPU, against the reference library
-    itself on the host cores (bounded sample) on rank 0."""
+    on 8 slots x 30 layers x 32 heads per GPU (whole-job rate), against the
+    reference library itself on the host cores (bounded sample) on rank 0."""
     slots = 8
     heads = slots * LAYERS * HEADS
     states = codec.synthesize_states(slots, LAYERS, HEADS, layout=layout, seed=2,
@@ -660,7 +661,7 @@ def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, ra
     end.record(stream)
     barrier()
     ms = max_over_ranks(start.elapsed_time(end)) / iters
-    result = {"heads": heads, "ms": ms, "states_per_s": heads / (ms / 1e3),
+    result = {"heads_per_gpu": heads, "ms": ms, "states_per_s": world * heads / (ms / 1e3),
               "bit_exact_to": "FromDenseBoundary (tests/test_gpu_full.py)"}
     if rank == 0:
         result["cpu_reference"] = full_codec_cpu_reference()
