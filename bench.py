@@ -373,7 +373,8 @@ def main() -> None:
     box = box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
                       rank, world)
     torch.cuda.empty_cache()
-    decode = decode_measure(codec, torch, device, barrier, max_over_ranks, SLOTS, world=world)
+    decode = decode_measure(codec, torch, device, barrier, max_over_ranks, SLOTS, world=world,
+                            rank=rank)
     torch.cuda.empty_cache()
 
     if rank == 0:
@@ -544,8 +545,51 @@ def decode_step_bytes(position: float) -> float:
             + 256 + 256 + 2 + 4 + 256)
 
 
+def decode_cpu_reference(sample_heads: int = 256, tokens: int = 15,
+                         target_seconds: float = 0.2):
+    """ApplyToken of the reference library (oracle/_ref, native/src) on the
+    host cores: `tokens` Qwen3.5-like tokens (positions 0..14, no window
+    crossing) per head over a bounded sample of heads, each head's capsule
+    made by FromDenseBoundary first (not timed).  The rate is head-steps per
+    second of ApplyToken time per thread, times the threads used."""
+    import concurrent.futures
+
+    import numpy as np
+    import oracle as oracle_mod  # noqa: PLC0415 - baseline only
+
+    if not oracle_mod.ref_available():
+        return None
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(11)
+    cases = []
+    for _ in range(sample_heads):
+        dense = (rng.standard_normal((128, 128)) * 10.0 ** (-3.0 * rng.random())).astype(np.float32)
+        decay = np.exp(-(0.005 + 0.095 * rng.random(tokens))).astype(np.float32)
+        k = rng.standard_normal((tokens, 128)).astype(np.float32)
+        k /= np.linalg.norm(k, axis=1, keepdims=True)
+        beta = rng.random(tokens).astype(np.float32)
+        q = rng.standard_normal((tokens, 128)).astype(np.float32)
+        q *= np.float32(128 ** -0.5) / np.linalg.norm(q, axis=1, keepdims=True)
+        v = rng.standard_normal((tokens, 128)).astype(np.float32)
+        cases.append((dense, decay, (beta[:, None] * k).astype(np.float32),
+                      (decay[:, None] * k).astype(np.float32), q, v))
+    busy, steps, t0 = 0.0, 0, time.perf_counter()
+    with concurrent.futures.ThreadPoolExecutor(max_workers=cores) as pool:
+        while True:
+            busy += sum(pool.map(lambda c: oracle_mod.ref_time_apply_tokens(*c), cases))
+            steps += sample_heads * tokens
+            if busy >= target_seconds * cores or time.perf_counter() - t0 > 20.0:
+                break
+    per_thread = steps / busy
+    return {"head_steps_per_s": per_thread * cores, "per_thread_head_steps_per_s": per_thread,
+            "cores": cores, "kind": "reference",
+            "sample": f"{steps} head-steps ({sample_heads} heads x {tokens} tokens, ApplyToken "
+                      f"of oracle/_ref/libgdn_ref.so, fp32 records) on {cores} threads, "
+                      f"{time.perf_counter() - t0:.2f} s wall"}
+
+
 def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows: int = 4,
-                   timed: bool = True, world: int = 1):
+                   timed: bool = True, world: int = 1, rank: int = 0):
     """The Qwen3.5 windowed decode on `slots` x 30 layers x 32 heads per GPU
     (provider layout, quant-only boundary, the plugin's default): each window
     is 16 bf16 decode steps over every head then the quant-only boundary
@@ -630,7 +674,8 @@ def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows
     barrier()
     dense_ms = max_over_ranks(start.elapsed_time(end) / steps)
     del dense
-    return {"heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
+    cpu = decode_cpu_reference() if rank == 0 else None
+    return {"cpu_reference": cpu, "heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
             "windows": windows, "step_ms": step, "step_ms_at_position": {"0": by_position[0],
                                                                       "15": by_position[1]},
             "head_steps_per_s": world * heads / (step / 1e3),

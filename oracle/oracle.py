@@ -602,3 +602,22 @@ def ref_window_read(head: "WindowHead", x: np.ndarray) -> np.ndarray:
     if status != 0:
         raise ValueError("reference window read rejected the input")
     return out
+
+
+def ref_time_apply_tokens(dense: np.ndarray, decay, key, read, query, value) -> float:
+    """Seconds the reference library spends in ApplyToken for these tokens
+    (after FromDenseBoundary(dense), which is not timed)."""
+    handle = ref()
+    if not hasattr(handle, "_time_ready"):
+        u32 = ctypes.c_uint32
+        handle.ref_time_apply_tokens.argtypes = [
+            _f32p, u32, u32, u32, _f32p, _f32p, _f32p, _f32p, _f32p]
+        handle.ref_time_apply_tokens.restype = ctypes.c_double
+        handle._time_ready = True
+    dense = np.ascontiguousarray(dense, np.float32)
+    arrays = [np.ascontiguousarray(a, np.float32) for a in (decay, key, read, query, value)]
+    seconds = handle.ref_time_apply_tokens(_ptr(dense, _f32p), 128, 128, arrays[0].shape[0],
+                                           *[_ptr(a, _f32p) for a in arrays])
+    if seconds < 0:
+        raise ValueError("reference rejected the token sequence")
+    return float(seconds)

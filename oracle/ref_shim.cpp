@@ -14,6 +14,7 @@
 //   GdnStateCodecCapsule::DenseState         (capsule.cpp:337-352)
 //   GdnStateCodecCapsule::ApplyToken         (capsule.cpp:354-397)
 // and the Qwen layout adapter (gdn_state_codec_qwen38_gdn_adapter.h:10-17).
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -240,5 +241,41 @@ extern "C" int ref_apply_tokens(const float* dense, std::uint32_t keys, std::uin
     return 0;
   } catch (const std::exception&) {
     return 1;
+  }
+}
+
+// Seconds spent inside `tokens` ApplyToken calls (capsule.cpp:354-397) on a
+// capsule made by FromDenseBoundary(dense), timed with a steady clock around
+// the token loop only (the boundary fit before it is not timed).  Token t
+// uses the scalar decay decay[t] broadcast over the keys.  Returns a negative
+// value when the reference rejects an input.  Used as the CPU baseline of the
+// decode step.
+extern "C" double ref_time_apply_tokens(const float* dense, std::uint32_t keys,
+                                        std::uint32_t values, std::uint32_t tokens,
+                                        const float* decay, const float* key, const float* read,
+                                        const float* query, const float* value) {
+  try {
+    const std::size_t elements = static_cast<std::size_t>(keys) * values;
+    std::vector<float> state(dense, dense + elements);
+    auto capsule = GdnStateCodecCapsule::FromDenseBoundary(
+        state, Identity(keys, values), GdnStateCodecParameters{});
+    std::vector<GdnStateCodecTokenInput> inputs(tokens);
+    for (std::uint32_t t = 0; t < tokens; ++t) {
+      auto& token = inputs[t];
+      token.decay.assign(keys, decay[t]);
+      token.key.assign(key + static_cast<std::size_t>(t) * keys,
+                       key + static_cast<std::size_t>(t + 1) * keys);
+      token.read.assign(read + static_cast<std::size_t>(t) * keys,
+                        read + static_cast<std::size_t>(t + 1) * keys);
+      token.query.assign(query + static_cast<std::size_t>(t) * keys,
+                         query + static_cast<std::size_t>(t + 1) * keys);
+      token.value.assign(value + static_cast<std::size_t>(t) * values,
+                         value + static_cast<std::size_t>(t + 1) * values);
+    }
+    const auto begin = std::chrono::steady_clock::now();
+    for (std::uint32_t t = 0; t < tokens; ++t) (void)capsule.ApplyToken(inputs[t]);
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - begin).count();
+  } catch (const std::exception&) {
+    return -1.0;
   }
 }
