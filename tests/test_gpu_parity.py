@@ -109,8 +109,11 @@ def test_encoded_projection(batch, layout):
                           to_np(q.float()).reshape(-1, 128), layout=layout, threads=8)
     got = to_np(out).reshape(-1, 128)
     assert_close_and_exact("projection", got, want)
-    # The fused readout also equals dequantize-then-matvec computed in fp64,
-    # within the fp32 tolerance.
+    # The fused readout also agrees with dequantize-then-matvec computed in
+    # fp64: a different order of the same sums over fp32-rounded dense
+    # values, so the agreement is to fp32 accumulation error (1e-4 relative),
+    # not bit for bit; the bit-exact target is the reference's own readout
+    # order, checked above at rtol 1e-5 / atol 1e-6 and bit for bit.
     dense = to_np(codec.dequantize(enc)).reshape(-1, 128, 128).astype(np.float64)
     qd = to_np(q.float()).reshape(-1, 128).astype(np.float64)
     ref64 = (np.einsum("hkv,hk->hv", dense, qd) if layout == "capsule"
