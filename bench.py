@@ -59,6 +59,9 @@ def parse_args():
     parser.add_argument("--profile-decode", action="store_true",
                         help="device-resident decode windows only (16 steps + refit per "
                              "window), for ncu captures of the window kernels")
+    parser.add_argument("--profile-capsule", action="store_true",
+                        help="device-resident capsule serialize + restore only, for ncu "
+                             "captures of the capsule kernels")
     parser.add_argument("--profile-full", action="store_true",
                         help="device-resident full-codec launches only (fit + quantize), "
                              "warm-up + steps of them, for ncu captures of the fit kernel")
@@ -236,7 +239,8 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.warmup < 3 and not (args.profile or args.profile_full or args.profile_decode):
+    if args.warmup < 3 and not (args.profile or args.profile_full or args.profile_decode
+                                or args.profile_capsule):
         raise SystemExit("--warmup must be >= 3")
 
     import torch
@@ -308,6 +312,23 @@ def main() -> None:
         step()
     barrier()
 
+    if args.profile_capsule:
+        geometry = "0123456789abcdef" * 4
+        capsules = torch.empty((heads, codec.CAPSULE_BYTES), dtype=torch.uint8, device=device)
+        flat = codec.EncodedStates(encoded.codes.view(-1, 128, 128),
+                                   encoded.smoothing.view(-1, 128), encoded.scales.view(-1, 128),
+                                   layout)
+        for _ in range(args.steps):
+            codec.serialize_capsules(flat, geometry=geometry, generation=3, epoch=42,
+                                     out=capsules)
+            codec.restore_capsules(capsules, layout, geometry=geometry, generation=3, epoch=42)
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile_capsule": True, "heads": heads, "steps": args.steps}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     if args.profile:
         queries = codec.synthesize_queries(slots, LAYERS, HEADS, seed=1, device=device)
         outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
@@ -360,6 +381,10 @@ def main() -> None:
 
     # ---- full codec (rank-4 fit + int8 stage) on a smaller batch --------------
     full = full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, rank, world)
+
+    # ---- capsule wire format of the step's encodings ---------------------------
+    capsule = capsule_measure(codec, torch, encoded, heads, device, barrier, max_over_ranks,
+                              rank, world)
 
     # ---- end to end through the public API with host buffers -----------------
     e2e = e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
@@ -415,6 +440,7 @@ def main() -> None:
             },
             "e2e": e2e,
             "full_codec": full,
+            "capsule_format": capsule,
             "config4_ragged": ragged,
             "config5_box": box,
             "decode_window": decode,
@@ -543,6 +569,73 @@ def box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
 def decode_step_bytes(position: float) -> float:
     return (16384 + 512 + 512 + position * (256 + 256 + 4) + (256 + 256 + 4 + 4)
             + 256 + 256 + 2 + 4 + 256)
+
+
+def capsule_measure(codec, torch, encoded, heads, device, barrier, max_over_ranks, rank,
+                    world):
+    """The capsule wire format (Serialize / Restore, capsule.cpp:446-578) of
+    every head the benchmark step encoded (quant-only boundary: zero
+    compensator planes): GPU serialize and fail-closed restore rates, and the
+    reference library's own Serialize / Restore on the host cores."""
+    geometry = "0123456789abcdef" * 4
+    flat = codec.EncodedStates(encoded.codes.view(-1, 128, 128), encoded.smoothing.view(-1, 128),
+                               encoded.scales.view(-1, 128), encoded.layout)
+    capsules = torch.empty((heads, codec.CAPSULE_BYTES), dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def serialize():
+        codec.serialize_capsules(flat, geometry=geometry, generation=3, epoch=42, out=capsules)
+
+    def restore():
+        return codec.restore_capsules(capsules, encoded.layout, geometry=geometry,
+                                      generation=3, epoch=42)
+
+    for _ in range(2):
+        serialize()
+        restored = restore()
+    ok = bool(torch.equal(restored[0].codes, flat.codes)) and int(restored[3].abs().sum()) == 0
+    del restored
+    barrier()
+    iters = 10
+    ser_ms = max_over_ranks(_timed(torch, stream, serialize, iters))
+    res_ms = max_over_ranks(_timed(torch, stream, restore, iters))
+    barrier()
+    ser_bytes = 17408 + codec.CAPSULE_BYTES
+    res_bytes = codec.CAPSULE_BYTES + 17408 + 4096
+    result = {"heads_per_gpu": heads, "capsule_bytes": codec.CAPSULE_BYTES,
+              "serialize_ms": ser_ms, "serialize_states_per_s": world * heads / (ser_ms / 1e3),
+              "serialize_gbs_per_gpu": ser_bytes * heads / (ser_ms / 1e3) / 1e9,
+              "restore_ms": res_ms, "restore_states_per_s": world * heads / (res_ms / 1e3),
+              "restore_gbs_per_gpu": res_bytes * heads / (res_ms / 1e3) / 1e9,
+              "round_trip_bit_exact": ok}
+    if rank == 0:
+        result["cpu_reference"] = capsule_cpu_reference()
+    return result
+
+
+def capsule_cpu_reference(sample_heads: int = 64, reps: int = 8):
+    """Serialize / Restore of the reference library (oracle/_ref) on the host
+    cores over a bounded sample; rates are per-thread rates times threads."""
+    import concurrent.futures
+
+    import numpy as np
+    import oracle as oracle_mod  # noqa: PLC0415 - baseline only
+
+    if not oracle_mod.ref_available():
+        return None
+    cores = os.cpu_count() or 1
+    heads = sample_states("capsule", sample_heads)
+    t0 = time.perf_counter()
+    with concurrent.futures.ThreadPoolExecutor(max_workers=cores) as pool:
+        times = list(pool.map(lambda h: oracle_mod.ref_time_capsule(h, reps), heads))
+    ser = sum(t[0] for t in times)
+    res = sum(t[1] for t in times)
+    calls = sample_heads * reps
+    return {"serialize_states_per_s": calls / ser * cores, "restore_states_per_s": calls / res * cores,
+            "cores": cores, "kind": "reference",
+            "sample": f"{calls} Serialize and {calls} Restore calls ({sample_heads} heads x {reps}) "
+                      f"of oracle/_ref/libgdn_ref.so on {cores} threads, "
+                      f"{time.perf_counter() - t0:.2f} s wall"}
 
 
 def decode_cpu_reference(sample_heads: int = 256, tokens: int = 15,

@@ -18,8 +18,10 @@
 // capsule with coalesced 8-byte stores, then a thread per head hashes it
 // (SHA-256 is sequential within a message and independent across heads).
 // Restore checks each capsule in the reference's order and reports the first
-// failing check per head; a thread per head hashes, validates, writes the
-// planes and checks that the dense state they encode is finite.
+// failing check per head: a thread per head checks the header and the
+// SHA-256 digest, then a CTA per head whose header passed checks the payload
+// and the finiteness of the dense state it encodes, and writes the boundary
+// only when every check passed.
 //
 // SHA-256 follows FIPS 180-4 (sections 4.1.2, 5.1.1, 6.2.2).  Its constants
 // are derived on the host from their definition -- the first 32 fractional
@@ -358,7 +360,11 @@ __device__ __forceinline__ uint64_t get_u64(const uint8_t* p) {
 }
 __device__ __forceinline__ float get_f32(const uint8_t* p) { return __uint_as_float(get_u32(p)); }
 
-__device__ int32_t restore_check(const uint8_t* c, const CapsuleIdentity& id) {
+// Restore, part 1 (thread per capsule): the header checks and the SHA-256
+// digest, which is sequential within a capsule -- checks 1 to 6 of
+// capsule.cpp:477-578 in the reference's order.  Returns the first failing
+// one, or kCapsuleOk when the payload checks may proceed.
+__device__ int32_t restore_header_check(const uint8_t* c, const CapsuleIdentity& id) {
   const char magic[8] = {'L', 'Q', 'C', 'A', 'P', 'S', '0', '1'};
   for (int i = 0; i < 8; ++i) {
     if (c[i] != static_cast<uint8_t>(magic[i])) return kCapsuleMagic;
@@ -384,63 +390,140 @@ __device__ int32_t restore_check(const uint8_t* c, const CapsuleIdentity& id) {
   for (int i = 0; i < 64; ++i) same = same && c[56 + i] == static_cast<uint8_t>(id.geometry[i]);
   if (!same) return kCapsuleIdentity;
   if (get_u32(c + 52) != 0u) return kCapsuleWindow;  // this format has no update records
-  const uint8_t* codes = c + kCapsuleHeader;
-  for (int i = 0; i < kElements; ++i) {
-    if (codes[i] == 0x80u) return kCapsuleCode;
-  }
-  const uint8_t* planes = codes + kElements;
-  for (int i = 0; i < kKeys; ++i) {
-    const float v = get_f32(planes + 4 * i);
-    if (!isfinite(v) || !(v > 0.0F)) return kCapsulePayloadBad;
-  }
-  for (int i = 0; i < kValues; ++i) {
-    const float v = get_f32(planes + 4 * (kKeys + i));
-    if (!isfinite(v) || !(v >= 0.0F)) return kCapsulePayloadBad;
-  }
-  for (int i = 0; i < kRank * (kKeys + kValues); ++i) {
-    if (!isfinite(get_f32(planes + 4 * (kKeys + kValues + i)))) return kCapsulePayloadBad;
-  }
-  // DenseState() must be finite (capsule.cpp:574-576): ((c * z) / 127) * b
-  // plus sum_r K V, in the reference's order.
-  const uint8_t* kp = planes + 4 * (kKeys + kValues);
-  const uint8_t* vp = kp + 4 * kKeys * kRank;
-  for (int k = 0; k < kKeys; ++k) {
-    const float ck = get_f32(planes + 4 * k);
-    float kr[kRank];
-    for (int r = 0; r < kRank; ++r) kr[r] = get_f32(kp + 4 * (k * kRank + r));
-    for (int v = 0; v < kValues; ++v) {
-      const float z = static_cast<float>(static_cast<int8_t>(codes[k * kValues + v]));
-      float value = __fmul_rn(__fdiv_rn(__fmul_rn(ck, z), kQuantMax),
-                              get_f32(planes + 4 * (kKeys + v)));
-      for (int r = 0; r < kRank; ++r) {
-        value = __fadd_rn(value, __fmul_rn(kr[r], get_f32(vp + 4 * (v * kRank + r))));
-      }
-      if (!isfinite(value)) return kCapsuleDense;
-    }
-  }
   return kCapsuleOk;
 }
 
-__global__ void __launch_bounds__(kCapsuleThreads) capsule_restore_kernel(RestoreParams p) {
-  const uint64_t head = static_cast<uint64_t>(blockIdx.x) * kCapsuleThreads + threadIdx.x;
+constexpr int kVerifyThreads = 64;
+
+__global__ void __launch_bounds__(kVerifyThreads) capsule_verify_kernel(RestoreParams p) {
+  const uint64_t head = static_cast<uint64_t>(blockIdx.x) * kVerifyThreads + threadIdx.x;
   if (head >= p.heads) return;
-  const uint8_t* c = p.capsules + head * kCapsuleBytes;
-  const int32_t status = restore_check(c, p.id);
-  p.head_status[head] = status;
-  if (status != kCapsuleOk) return;  // fail closed: nothing is written for this head
-  const uint8_t* codes = c + kCapsuleHeader;
-  int8_t* out = p.codes + head * kElements;
-  for (int i = 0; i < kElements; ++i) {
-    const int k = i / kValues, v = i % kValues;
-    out[p.provider ? v * kKeys + k : i] = static_cast<int8_t>(codes[i]);
-  }
-  const uint8_t* planes = codes + kElements;
-  for (int i = 0; i < kKeys; ++i) p.smoothing[head * kKeys + i] = get_f32(planes + 4 * i);
-  for (int i = 0; i < kValues; ++i) p.scales[head * kValues + i] = get_f32(planes + 4 * (kKeys + i));
-  for (int i = 0; i < kKeys * kRank; ++i) {
-    p.compensator_keys[head * kKeys * kRank + i] = get_f32(planes + 4 * (kKeys + kValues + i));
-    p.compensator_values[head * kValues * kRank + i] =
-        get_f32(planes + 4 * (kKeys + kValues + kKeys * kRank + i));
+  p.head_status[head] = restore_header_check(p.capsules + head * kCapsuleBytes, p.id);
+}
+
+// Restore, part 2 (a 128-thread CTA per capsule whose header checks passed):
+// checks 7 to 9 -- no code is -128; smoothing finite and positive, scales
+// finite and non-negative, compensators finite; the dense state the capsule
+// encodes (((c z) / 127) b + sum_r K V, the reference's order) finite --
+// reported in that order, and only when all pass are the codes and planes
+// written (fail closed).  Thread t scans codes row t (key t) and owns plane
+// entry t.
+struct __align__(16) RestoreShared {
+  int8_t codes[kElements];   // [key][value] as in the capsule
+  float b[kValues];          // scales
+  float4 v[kValues];         // compensator values
+  float4 bound[kCapsuleThreads / 32];  // per-warp max |c|, |b|, |K|, |V|
+};
+
+__global__ void __launch_bounds__(kCapsuleThreads) capsule_payload_kernel(RestoreParams p) {
+  __shared__ RestoreShared sh;
+  const int t = threadIdx.x;
+  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
+    if (__ldcg(p.head_status + head) != kCapsuleOk) continue;  // block-uniform
+    const uint8_t* c = p.capsules + head * kCapsuleBytes;
+    const uint8_t* codes = c + kCapsuleHeader;      // 8-byte aligned
+    const uint8_t* planes = codes + kElements;      // 8-byte aligned
+    // -- codes to shared memory, checking for -128 ----------------------------
+    bool bad_code = false;
+#pragma unroll 4
+    for (int i = t; i < kElements / 8; i += kCapsuleThreads) {
+      const uint2 w = __ldcs(reinterpret_cast<const uint2*>(codes) + i);
+      bad_code = bad_code || (__vcmpeq4(w.x, 0x80808080u) | __vcmpeq4(w.y, 0x80808080u)) != 0u;
+      reinterpret_cast<uint2*>(sh.codes)[i] = w;
+    }
+    // -- planes of entry t ----------------------------------------------------
+    const float* f = reinterpret_cast<const float*>(planes);  // 4-byte aligned
+    const float smooth = f[t];
+    const float scale = f[kKeys + t];
+    const float* kp = f + kKeys + kValues;
+    const float* vp = kp + kKeys * kRank;
+    const float4 kr = make_float4(kp[4 * t], kp[4 * t + 1], kp[4 * t + 2], kp[4 * t + 3]);
+    const float4 vr = make_float4(vp[4 * t], vp[4 * t + 1], vp[4 * t + 2], vp[4 * t + 3]);
+    const bool bad_payload =
+        !isfinite(smooth) || !(smooth > 0.0F) || !isfinite(scale) || !(scale >= 0.0F) ||
+        !isfinite(kr.x) || !isfinite(kr.y) || !isfinite(kr.z) || !isfinite(kr.w) ||
+        !isfinite(vr.x) || !isfinite(vr.y) || !isfinite(vr.z) || !isfinite(vr.w);
+    sh.b[t] = scale;
+    sh.v[t] = vr;
+    const bool any_code = __syncthreads_or(bad_code) != 0;
+    const bool any_payload = __syncthreads_or(bad_payload) != 0;
+    // -- DenseState finite (capsule.cpp:574-576) --------------------------------
+    // With finite planes every element is at most (max|c| max|b| + 4 max|K|
+    // max|V|) times the growth of its eight roundings, far below FLT_MAX when
+    // that bound is below 1e38; only a larger bound needs the element check
+    // (row t per thread, in the reference's order).
+    bool any_dense = false;
+    if (!any_code && !any_payload) {
+      float mc = fabsf(smooth), mb = fabsf(scale);
+      float mk = fmaxf(fmaxf(fabsf(kr.x), fabsf(kr.y)), fmaxf(fabsf(kr.z), fabsf(kr.w)));
+      float mv = fmaxf(fmaxf(fabsf(vr.x), fabsf(vr.y)), fmaxf(fabsf(vr.z), fabsf(vr.w)));
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+        mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, off));
+        mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, off));
+      }
+      if ((t & 31) == 0) sh.bound[t >> 5] = make_float4(mc, mb, mk, mv);
+      __syncthreads();
+      float4 m = sh.bound[0];
+#pragma unroll
+      for (int w = 1; w < kCapsuleThreads / 32; ++w) {
+        const float4 o = sh.bound[w];
+        m = make_float4(fmaxf(m.x, o.x), fmaxf(m.y, o.y), fmaxf(m.z, o.z), fmaxf(m.w, o.w));
+      }
+      const double bound = static_cast<double>(m.x) * m.y + 4.0 * static_cast<double>(m.z) * m.w;
+      if (!(bound < 1.0e38)) {  // block-uniform
+        bool bad_dense = false;
+        for (int v = 0; v < kValues; ++v) {
+          const float z = static_cast<float>(sh.codes[t * kValues + v]);
+          float value = __fmul_rn(div127_any(__fmul_rn(smooth, z)), sh.b[v]);
+          const float4 vv = sh.v[v];
+          value = __fadd_rn(value, __fmul_rn(kr.x, vv.x));
+          value = __fadd_rn(value, __fmul_rn(kr.y, vv.y));
+          value = __fadd_rn(value, __fmul_rn(kr.z, vv.z));
+          value = __fadd_rn(value, __fmul_rn(kr.w, vv.w));
+          bad_dense = bad_dense || !isfinite(value);
+        }
+        any_dense = __syncthreads_or(bad_dense) != 0;
+      }
+    }
+    const int32_t status = any_code      ? kCapsuleCode
+                           : any_payload ? kCapsulePayloadBad
+                           : any_dense   ? kCapsuleDense
+                                         : kCapsuleOk;
+    if (t == 0) p.head_status[head] = status;
+    if (status == kCapsuleOk) {
+      // -- write the boundary -------------------------------------------------
+      int8_t* out = p.codes + head * kElements;
+      if (!p.provider) {
+#pragma unroll 4
+        for (int i = t; i < kElements / 16; i += kCapsuleThreads) {
+          reinterpret_cast<uint4*>(out)[i] = reinterpret_cast<const uint4*>(sh.codes)[i];
+        }
+      } else {
+        // row v = t of the provider layout: codes [k][t] for k = 0..127
+        for (int k0 = 0; k0 < kKeys; k0 += 16) {
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              word |= static_cast<uint32_t>(static_cast<uint8_t>(
+                          sh.codes[(k0 + 4 * j + b) * kValues + t])) << (8 * b);
+            }
+            w[j] = word;
+          }
+          reinterpret_cast<uint4*>(out + t * kKeys + k0)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      p.smoothing[head * kKeys + t] = smooth;
+      p.scales[head * kValues + t] = scale;
+      reinterpret_cast<float4*>(p.compensator_keys)[head * kKeys + t] = kr;
+      reinterpret_cast<float4*>(p.compensator_values)[head * kValues + t] = vr;
+    }
+    __syncthreads();  // shared memory is reused by the next capsule
   }
 }
 

@@ -464,9 +464,12 @@ int32_t statecentric_gdn_state_codec_capsule_restore_launch_v1(
   gdnsc::RestoreParams p{capsules, codes, smoothing, scales, compensator_keys,
                          compensator_values, head_status, states, static_cast<int>(layout),
                          gdnsc::make_identity(model_geometry_sha256, generation, epoch)};
-  const unsigned grid = (states + gdnsc::kCapsuleThreads - 1) / gdnsc::kCapsuleThreads;
-  gdnsc::capsule_restore_kernel<<<grid, gdnsc::kCapsuleThreads, 0,
-                                  static_cast<cudaStream_t>(stream)>>>(p);
+  const auto st = static_cast<cudaStream_t>(stream);
+  const unsigned verify_grid = (states + gdnsc::kVerifyThreads - 1) / gdnsc::kVerifyThreads;
+  gdnsc::capsule_verify_kernel<<<verify_grid, gdnsc::kVerifyThreads, 0, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return gdnsc::kLaunchFailed;
+  gdnsc::capsule_payload_kernel<<<gdnsc::grid_for(states, s->sms, 8), gdnsc::kCapsuleThreads, 0,
+                                  st>>>(p);
   return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
 }
 

@@ -621,3 +621,21 @@ def ref_time_apply_tokens(dense: np.ndarray, decay, key, read, query, value) -> 
     if seconds < 0:
         raise ValueError("reference rejected the token sequence")
     return float(seconds)
+
+
+def ref_time_capsule(dense: np.ndarray, reps: int) -> tuple[float, float]:
+    """(Serialize seconds, Restore seconds) of the reference library for
+    `reps` calls each on the capsule of FromDenseBoundary(dense)."""
+    handle = ref()
+    if not hasattr(handle, "_capsule_time_ready"):
+        u32 = ctypes.c_uint32
+        dp = ctypes.POINTER(ctypes.c_double)
+        handle.ref_time_capsule.argtypes = [_f32p, u32, u32, u32, dp, dp]
+        handle.ref_time_capsule.restype = ctypes.c_int
+        handle._capsule_time_ready = True
+    dense = np.ascontiguousarray(dense, np.float32)
+    ser, res = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    if handle.ref_time_capsule(_ptr(dense, _f32p), 128, 128, reps, ctypes.byref(ser),
+                               ctypes.byref(res)) != 0:
+        raise ValueError("reference rejected the head")
+    return float(ser.value), float(res.value)

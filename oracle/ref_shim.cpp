@@ -279,3 +279,35 @@ extern "C" double ref_time_apply_tokens(const float* dense, std::uint32_t keys,
     return -1.0;
   }
 }
+
+// Seconds spent in `reps` Serialize calls (capsule.cpp:446-475) and in `reps`
+// Restore calls (:477-578) of the capsule FromDenseBoundary(dense) makes (the
+// fit itself is not timed), each timed with a steady clock.  Returns 0, or 1
+// when the reference rejects an input.  Used as the CPU baseline of the
+// capsule wire format.
+extern "C" int ref_time_capsule(const float* dense, std::uint32_t keys, std::uint32_t values,
+                                std::uint32_t reps, double* serialize_seconds,
+                                double* restore_seconds) {
+  try {
+    const std::size_t elements = static_cast<std::size_t>(keys) * values;
+    std::vector<float> state(dense, dense + elements);
+    const auto identity = Identity(keys, values);
+    const auto capsule =
+        GdnStateCodecCapsule::FromDenseBoundary(state, identity, GdnStateCodecParameters{});
+    std::vector<std::uint8_t> bytes;
+    auto begin = std::chrono::steady_clock::now();
+    for (std::uint32_t r = 0; r < reps; ++r) bytes = capsule.Serialize();
+    *serialize_seconds =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - begin).count();
+    begin = std::chrono::steady_clock::now();
+    for (std::uint32_t r = 0; r < reps; ++r) {
+      (void)GdnStateCodecCapsule::Restore(std::span<const std::uint8_t>(bytes), identity,
+                                          GdnStateCodecParameters{}, 0);
+    }
+    *restore_seconds =
+        std::chrono::duration<double>(std::chrono::steady_clock::now() - begin).count();
+    return 0;
+  } catch (const std::exception&) {
+    return 1;
+  }
+}
