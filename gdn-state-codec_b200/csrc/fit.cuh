@@ -22,8 +22,9 @@
 // reference's sequential order per output.  Norms sum the exact double
 // squares in a tree and fall back to the reference's sequential order when
 // the square root lies near a float rounding midpoint (the same proof as the
-// smoothing sums).  The singular value is one sequential 16,384-term chain
-// run by one thread; the other CTAs of the SM overlap it.  The residual the
+// smoothing sums).  The singular value is one sequential 16,384-term chain:
+// all threads form its products four rows at a time and one thread adds
+// them in order; the other CTAs of the SM overlap the chain.  The residual the
 // int8 stage encodes is written to a caller-provided workspace.
 #pragma once
 
@@ -54,10 +55,13 @@ struct FitParams {
   int provider;
 };
 
+constexpr int kSvRows = 4;  // rows of singular-value products formed per step
+
 struct __align__(16) FitShared {
   float r[kKeys][kFitStride];  // residual [key][value]
   float left[kKeys];
   float right[kValues];
+  float prod[kSvRows][kValues];  // singular-value products of kSvRows rows
   double part[kFitThreads / 32];
   float norm;               // broadcast of a norm or of the singular value
 };
@@ -134,8 +138,15 @@ __device__ __forceinline__ void fit_ranks(FitShared& sh, int t, int iterations, 
       // right[t] = sum_k R[k][t] * left[k], k = 0..127 in order.
       {
         float acc = 0.0F;
-#pragma unroll 8
-        for (int k = 0; k < kKeys; ++k) acc = __fadd_rn(acc, __fmul_rn(sh.r[k][t], sh.left[k]));
+        const float4* lft = reinterpret_cast<const float4*>(sh.left);
+#pragma unroll 4
+        for (int k4 = 0; k4 < kKeys / 4; ++k4) {
+          const float4 l = lft[k4];
+          acc = __fadd_rn(acc, __fmul_rn(sh.r[4 * k4][t], l.x));
+          acc = __fadd_rn(acc, __fmul_rn(sh.r[4 * k4 + 1][t], l.y));
+          acc = __fadd_rn(acc, __fmul_rn(sh.r[4 * k4 + 2][t], l.z));
+          acc = __fadd_rn(acc, __fmul_rn(sh.r[4 * k4 + 3][t], l.w));
+        }
         rv = acc;
         sh.right[t] = rv;  // right[] is not read by this sweep
       }
@@ -144,23 +155,34 @@ __device__ __forceinline__ void fit_ranks(FitShared& sh, int t, int iterations, 
     }
     __syncthreads();
     // -- singular value: one sequential chain in row-major order -----------
-    if (t == 0) {
-      float sv = 0.0F;
-      const float4* rgt = reinterpret_cast<const float4*>(sh.right);
-      for (int k = 0; k < kKeys; ++k) {
-        const float l = sh.left[k];
-        const float4* row = reinterpret_cast<const float4*>(sh.r[k]);
-#pragma unroll 8
-        for (int c4 = 0; c4 < kValues / 4; ++c4) {
-          const float4 a = row[c4], b = rgt[c4];
-          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.x), b.x));
-          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.y), b.y));
-          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.z), b.z));
-          sv = __fadd_rn(sv, __fmul_rn(__fmul_rn(l, a.w), b.w));
+    // All threads form the products (left[k] R[k][c]) right[c] of kSvRows
+    // rows at a time (thread t: column t); thread 0 adds them in order.
+    {
+      float sv = 0.0F;  // thread 0's running sum
+      const float rt = sh.right[t];
+      for (int k0 = 0; k0 < kKeys; k0 += kSvRows) {
+#pragma unroll
+        for (int j = 0; j < kSvRows; ++j) {
+          sh.prod[j][t] = __fmul_rn(__fmul_rn(sh.left[k0 + j], sh.r[k0 + j][t]), rt);
         }
+        __syncthreads();
+        if (t == 0) {
+          const float4* pr = reinterpret_cast<const float4*>(&sh.prod[0][0]);
+#pragma unroll 8
+          for (int i = 0; i < kSvRows * kValues / 4; ++i) {
+            const float4 q = pr[i];
+            sv = __fadd_rn(sv, q.x);
+            sv = __fadd_rn(sv, q.y);
+            sv = __fadd_rn(sv, q.z);
+            sv = __fadd_rn(sv, q.w);
+          }
+        }
+        __syncthreads();
       }
-      if (!isfinite(sv)) report(status, kStatusNonFinite);
-      sh.norm = sv;
+      if (t == 0) {
+        if (!isfinite(sv)) report(status, kStatusNonFinite);
+        sh.norm = sv;
+      }
     }
     __syncthreads();
     const float sv = sh.norm;
