@@ -75,22 +75,20 @@ __device__ __forceinline__ bool fit_normalize(FitShared& sh, float* vec, float& 
   for (int off = 16; off >= 1; off >>= 1) sq = __dadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, off));
   if ((t & 31) == 0) sh.part[t >> 5] = sq;
   __syncthreads();
-  if (t == 0) {
-    const double tree = __dadd_rn(__dadd_rn(sh.part[0], sh.part[1]), __dadd_rn(sh.part[2], sh.part[3]));
-    double root = __dsqrt_rn(tree);
-    if (near_float_midpoint(root)) {
-      // The float norm could depend on the summation order: redo the sum in
-      // the reference's order (element 0..127).
-      double seq = 0.0;
-      for (int i = 0; i < kKeys; ++i) {
-        seq = __dadd_rn(seq, static_cast<double>(vec[i]) * static_cast<double>(vec[i]));
-      }
-      root = __dsqrt_rn(seq);
+  // Every thread forms the same norm from the same partials (no broadcast).
+  const double tree = __dadd_rn(__dadd_rn(sh.part[0], sh.part[1]), __dadd_rn(sh.part[2], sh.part[3]));
+  double root = __dsqrt_rn(tree);
+  if (near_float_midpoint(root)) {  // block-uniform
+    // The float norm could depend on the summation order: redo the sum in
+    // the reference's order (element 0..127).
+    double seq = 0.0;
+    for (int i = 0; i < kKeys; ++i) {
+      seq = __dadd_rn(seq, static_cast<double>(vec[i]) * static_cast<double>(vec[i]));
     }
-    sh.norm = __double2float_rn(root);
+    root = __dsqrt_rn(seq);
+    __syncthreads();  // every thread has read vec before any thread rescales it
   }
-  __syncthreads();
-  const float norm = sh.norm;
+  const float norm = __double2float_rn(root);
   if (!(norm > 1.1920928955078125e-07F)) return false;  // FLT_EPSILON
   v = __fdiv_rn(v, norm);
   vec[t] = v;
