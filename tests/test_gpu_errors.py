@@ -64,3 +64,44 @@ def test_python_api_validation():
     enc = codec.quantize(states)
     with pytest.raises(ValueError):
         codec.encoded_projection(enc, torch.zeros(2, 128, device=DEV))  # fp32 query
+
+
+def test_window_api_validation():
+    """The window API refuses what its kernels cannot take, before any launch."""
+    codec.device_error(DEV, clear=True)
+    states = codec.synthesize_states(1, 1, 4, layout="provider", device=DEV).reshape(4, 128, 128)
+    enc = codec.quantize(states, "provider")
+    window = codec.new_window(enc)
+    bf = torch.bfloat16
+    token = dict(log_decay=torch.zeros(4, device=DEV), beta=torch.zeros(4, dtype=bf, device=DEV),
+                 keys=torch.zeros(2, 128, dtype=bf, device=DEV),
+                 queries=torch.zeros(2, 128, dtype=bf, device=DEV),
+                 values=torch.zeros(4, 128, dtype=bf, device=DEV))
+    codec.window_step_bf16(window, **token)  # valid
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError, match="one value per head"):
+        codec.window_step_bf16(window, **{**token, "log_decay": torch.zeros(3, device=DEV)})
+    with pytest.raises(ValueError):
+        codec.window_step_bf16(window, **{**token, "keys": torch.zeros(4, 128, dtype=bf, device=DEV)})
+    with pytest.raises(ValueError):
+        codec.window_step_bf16(window, **{**token, "values": token["values"].float()})
+    odd = codec.new_window(codec.quantize(states[:3].contiguous(), "provider"))
+    with pytest.raises(ValueError, match="even number of heads"):
+        codec.window_step_bf16(odd, **token)
+    capsule = codec.new_window(codec.quantize(states, "capsule"))
+    with pytest.raises(ValueError, match="provider-layout"):
+        codec.window_step_bf16(capsule, **token)
+    with pytest.raises(ValueError, match="needs compensators"):
+        codec.window_step(capsule, torch.ones(4, device=DEV),
+                          *[torch.zeros(4, 128, dtype=torch.float16, device=DEV)] * 4)
+    with pytest.raises(ValueError, match="power_iterations"):
+        codec.window_refit(window, 33)
+    with pytest.raises(ValueError, match="provider-layout"):
+        codec.window_refit(capsule, 0)
+    with pytest.raises(ValueError, match="go together"):
+        codec.new_window(enc, torch.zeros(4, 128, 4, dtype=torch.float16, device=DEV), None)
+    with pytest.raises(ValueError):
+        codec.new_window(enc, torch.zeros(4, 128, 4, device=DEV),
+                         torch.zeros(4, 128, 4, device=DEV))  # fp32, not binary16
+    # nothing above reached the device with bad arguments
+    assert codec.device_error(DEV) & ~codec.STATUS_WINDOW_FULL == 0
