@@ -21,8 +21,7 @@
  *    value scales are per value [128], compensators are [128][4] fp32.
  *  - Return values: 0 = enqueued; 1 = rejected arguments (null pointer,
  *    zero count, misalignment, bad layout flag); 2 = the CUDA launch failed;
- *    3 = device query or kernel set-up failed; 5 = entry point exists only
- *    for loader compatibility and is not implemented by this backend.
+ *    3 = device query or kernel set-up failed.
  *  - `states` may be any value >= 1 (the reference's Ascend launchers
  *    capped it at 64 per launch; this is a documented superset).
  *  - Results are bit-identical to the reference's portable C++ codec

@@ -47,7 +47,6 @@ REFERENCE_LIBRARIES = {
 }
 
 BAD_ARGS = 1
-NOT_IMPLEMENTED = 5
 ALIGNED = 0x10000  # fake, 16-byte aligned, never dereferenced
 MISALIGNED = 0x10004
 
