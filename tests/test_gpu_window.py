@@ -245,3 +245,54 @@ def test_refit_of_a_partial_window_matches_oracle(compensators, iterations):
     _assert_boundary(nxt, heads, f"partial refit ({iterations})")
     check_records(nxt, heads, "partial refit")
     assert (nxt.compensator_keys is None) == (not compensators and iterations == 0)
+
+
+def test_generic_step_sequence_matches_oracle():
+    """16 generic (binary16) tokens from an empty window over a rank-4
+    boundary, capsule layout: every output and record bit-identical to the
+    oracle, the window full at the end."""
+    nheads = 8
+    states = codec.synthesize_states(1, 1, nheads, layout="capsule", seed=61,
+                                     device=DEV).reshape(nheads, 128, 128)
+    full = codec.full_encode(states, "capsule")
+    window = codec.new_window(full.encoded, full.compensator_keys.half().contiguous(),
+                              full.compensator_values.half().contiguous())
+    heads = _oracle_heads_capsule(window)
+    rng = np.random.default_rng(62)
+    for t in range(wc.WINDOW):
+        decay = (0.9 + 0.1 * rng.random(nheads)).astype(np.float32)
+        vec = lambda s: wc.f16(rng.standard_normal((nheads, 128)) * s)  # noqa: E731
+        key, read, query, value = vec(0.09), vec(0.09), vec(0.09), vec(1.0)
+        out = codec.window_step(window, f32_dev(decay), f16_dev(key), f16_dev(read),
+                                f16_dev(query), f16_dev(value))
+        want = np.stack([h.step(decay[i], key[i], read[i], query[i], value[i])
+                         for i, h in enumerate(heads)])
+        assert np.array_equal(bits(out.cpu().numpy()), bits(want)), f"token {t}"
+        check_records(window, heads, f"token {t}")
+    assert bool((window.positions[:, 0] == wc.WINDOW).all())
+
+
+def _oracle_heads_capsule(window):
+    torch.cuda.synchronize()
+    enc = window.encoded
+    codes, c, b = enc.codes.cpu().numpy(), enc.smoothing.cpu().numpy(), enc.scales.cpu().numpy()
+    ck = window.compensator_keys.float().cpu().numpy()
+    cv = window.compensator_values.float().cpu().numpy()
+    return [oracle.WindowHead(codes[i], c[i], b[i], ck[i], cv[i], layout="capsule")
+            for i in range(codes.shape[0])]
+
+
+def test_non_finite_token_sets_the_status_bit():
+    nheads = 4
+    window = _qwen_boundary(nheads, False, seed=71)
+    inputs = wc.qwen_tokens(nheads, 1, seed=72)
+    values = inputs["values"][0].copy()
+    values[1, 5] = 0x7FC0  # bf16 NaN in head 1
+    codec.device_error(DEV, clear=True)
+    out = codec.window_step_bf16(window, f32_dev(inputs["log_decay"][0]),
+                                 bf16_dev(inputs["beta"][0]), bf16_dev(inputs["keys"][0]),
+                                 bf16_dev(inputs["queries"][0]), bf16_dev(values))
+    torch.cuda.synchronize()
+    assert codec.device_error(DEV, clear=True) & 4
+    assert torch.isnan(out[1].float()).any()
+    assert torch.isfinite(out[0].float()).all() and torch.isfinite(out[2:].float()).all()
