@@ -681,6 +681,64 @@ def decode_cpu_reference(sample_heads: int = 256, tokens: int = 15,
                       f"{time.perf_counter() - t0:.2f} s wall"}
 
 
+def decode_token_latency(codec, torch, device, stream, tokens: int = 15):
+    """The plugin's decode shape: one request, 30 layers x 32 heads, one
+    bf16 step launch per layer per token (runtime.py:750-845).  Device time
+    per token of the 30 launches issued eagerly through the Python API, and
+    replayed from one CUDA graph that holds them."""
+    windows, inputs = [], []
+    gen = torch.Generator(device=device).manual_seed(21)
+    for layer in range(LAYERS):
+        states = codec.synthesize_states(1, 1, HEADS, layout="provider", seed=30 + layer,
+                                         device=device).reshape(HEADS, 128, 128)
+        windows.append(codec.new_window(codec.quantize(states, "provider")))
+        kq = torch.randn((2, HEADS // 2, 128), generator=gen, device=device)
+        inputs.append((-0.05 * torch.rand(HEADS, generator=gen, device=device),
+                       torch.rand(HEADS, generator=gen, device=device).to(torch.bfloat16),
+                       (kq[0] / kq[0].norm(dim=-1, keepdim=True)).to(torch.bfloat16),
+                       (kq[1] / kq[1].norm(dim=-1, keepdim=True)).to(torch.bfloat16),
+                       torch.randn((HEADS, 128), generator=gen, device=device).to(torch.bfloat16),
+                       torch.empty((HEADS, 128), dtype=torch.bfloat16, device=device)))
+
+    def token():
+        for window, (log_decay, beta, k, q, v, out) in zip(windows, inputs):
+            codec.window_step_bf16(window, log_decay, beta, k, q, v, out=out)
+
+    def reset():
+        for window in windows:
+            window.positions.zero_()
+
+    token()  # warm-up
+    reset()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(tokens):
+        token()
+    end.record(stream)
+    end.synchronize()
+    eager_us = start.elapsed_time(end) / tokens * 1e3
+    reset()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        token()
+    stream.wait_stream(side)
+    reset()
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(tokens):
+        graph.replay()
+    end.record(stream)
+    end.synchronize()
+    graph_us = start.elapsed_time(end) / tokens * 1e3
+    del graph
+    return {"layers": LAYERS, "heads_per_layer": HEADS, "tokens": tokens,
+            "eager_us_per_token": eager_us, "graph_us_per_token": graph_us,
+            "launches_per_token": LAYERS}
+
+
 def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows: int = 4,
                    timed: bool = True, world: int = 1, rank: int = 0):
     """The Qwen3.5 windowed decode on `slots` x 30 layers x 32 heads per GPU
@@ -768,7 +826,8 @@ def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows
     dense_ms = max_over_ranks(start.elapsed_time(end) / steps)
     del dense
     cpu = decode_cpu_reference() if rank == 0 else None
-    return {"cpu_reference": cpu, "heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
+    plugin = decode_token_latency(codec, torch, device, stream)
+    return {"cpu_reference": cpu, "plugin_shape_token": plugin, "heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
             "windows": windows, "step_ms": step, "step_ms_at_position": {"0": by_position[0],
                                                                       "15": by_position[1]},
             "head_steps_per_s": world * heads / (step / 1e3),
