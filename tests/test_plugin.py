@@ -282,3 +282,27 @@ def test_adapter_refuses_a_foreign_host(monkeypatch):
     monkeypatch.setitem(sys.modules, adapter._HOST_MODULE, module)
     with pytest.raises(RuntimeError, match="refuses an unsupported or already patched"):
         adapter.install()
+
+
+# -- spawned children ----------------------------------------------------------
+
+def test_child_entry_registers_before_the_target(monkeypatch):
+    from gdn_state_codec import bootstrap
+
+    calls = []
+    monkeypatch.setattr(plugin, "register", lambda: calls.append("register"))
+    result = bootstrap.child_entry(lambda *a, **k: calls.append(("target", a, k)) or "done",
+                                   1, key=2)
+    assert result == "done"
+    assert calls == ["register", ("target", (1,), {"key": 2})]
+
+
+def test_child_entry_runs_in_a_spawned_interpreter(monkeypatch):
+    import multiprocessing
+    import operator
+
+    from gdn_state_codec import bootstrap
+
+    _clear_switches(monkeypatch)
+    with multiprocessing.get_context("spawn").Pool(1) as pool:
+        assert pool.apply(bootstrap.child_entry, (operator.add, 2, 3)) == 5
