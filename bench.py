@@ -36,6 +36,9 @@ sys.path.insert(0, str(ROOT / "oracle"))  # CPU-baseline leg only (the checker)
 
 METRIC = "codec HBM GB/s (% of B200 peak) and states/sec at 1/2/4/8 B200"
 UNIT = "states/s"
+# CPU baselines are timed on rank 0 of the one-GPU run only (the host cores are
+# shared by every rank of a multi-GPU run).
+CPU_AT_N1 = "timed by the one-GPU run only"
 SLOTS, LAYERS, HEADS = 64, 30, 32
 BYTES_PER_HEAD = {  # algorithmic bytes per head (one launch of each kernel)
     "quantize": 65536 + 16384 + 512 + 512,
@@ -87,8 +90,9 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []   # (host monotonic time, csv line)
         self.thread = None
+        self.ready = threading.Event()
 
     def start(self) -> None:
         try:
@@ -104,11 +108,26 @@ class ClockSampler:
 
     def _read(self) -> None:
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+            self.ready.set()
 
-    def stop(self) -> dict:
+    def wait_ready(self, timeout_s: float = 20.0) -> None:
+        """Block until nvidia-smi emits its first sample (NVML start-up takes
+        longer on an 8-GPU box than a short timed region lasts)."""
+        if self.proc is not None:
+            self.ready.wait(timeout_s)
+
+    def stop(self, t0: float | None = None, t1: float | None = None) -> dict:
+        """Summarise the samples taken between host times t0 and t1 (the
+        timed region).  A region shorter than the sampling interval may hold
+        none; then the first sample after t0 stands in, and ``window`` says so."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        window = "timed region"
+        if t0 is not None:
+            deadline = time.monotonic() + 1.0
+            while not any(t >= t0 for t, _ in self.lines) and time.monotonic() < deadline:
+                time.sleep(0.02)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -116,9 +135,14 @@ class ClockSampler:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=5)
+        lines = [line for t, line in self.lines
+                 if (t0 is None or t >= t0) and (t1 is None or t <= t1)]
+        if not lines and t0 is not None:
+            lines = [line for t, line in self.lines if t >= t0][:1]
+            window = "first sample after the timed region began (region shorter than 100 ms)"
         sm, sm_max, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -136,6 +160,7 @@ class ClockSampler:
             "sm_max_mhz": max(sm_max) if sm_max else None,
             "power_w_max": max(power) if power else None,
             "samples": len(sm),
+            "window": window,
             "reasons": sorted(reasons),
         }
 
@@ -344,18 +369,19 @@ def main() -> None:
 
     sampler = ClockSampler(local_rank)
     sampler.start()
-    time.sleep(0.3)  # let the sampler attach before the timed region
+    sampler.wait_ready()
     per_step = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
                 for _ in range(args.steps)]
     barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    t0 = time.monotonic()
     start.record(stream)
     for i in range(args.steps):
         step(per_step[i])
     end.record(stream)
     barrier()
-    clocks = sampler.stop()
+    clocks = sampler.stop(t0, time.monotonic())
     elapsed_ms = max_over_ranks(start.elapsed_time(end))
     quant_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in per_step)
     deq_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in per_step)
@@ -447,7 +473,8 @@ def main() -> None:
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
         }
-        result["cpu_baseline"] = cpu_baseline(layout)
+        result["cpu_baseline"] = (cpu_baseline(layout) if world == 1 else
+                                  {"value": None, "unit": UNIT, "skipped": CPU_AT_N1})
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier()
@@ -608,8 +635,8 @@ def capsule_measure(codec, torch, encoded, heads, device, barrier, max_over_rank
               "restore_ms": res_ms, "restore_states_per_s": world * heads / (res_ms / 1e3),
               "restore_gbs_per_gpu": res_bytes * heads / (res_ms / 1e3) / 1e9,
               "round_trip_bit_exact": ok}
-    if rank == 0:
-        result["cpu_reference"] = capsule_cpu_reference()
+    result["cpu_reference"] = (capsule_cpu_reference() if world == 1
+                               else {"skipped": CPU_AT_N1})
     return result
 
 
@@ -825,7 +852,7 @@ def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows
     barrier()
     dense_ms = max_over_ranks(start.elapsed_time(end) / steps)
     del dense
-    cpu = decode_cpu_reference() if rank == 0 else None
+    cpu = decode_cpu_reference() if world == 1 else {"skipped": CPU_AT_N1}
     plugin = decode_token_latency(codec, torch, device, stream)
     return {"cpu_reference": cpu, "plugin_shape_token": plugin, "heads_per_gpu": heads, "layout": "provider", "boundary": "quant-only",
             "windows": windows, "step_ms": step, "step_ms_at_position": {"0": by_position[0],
@@ -860,8 +887,8 @@ def full_codec_measure(codec, torch, layout, device, barrier, max_over_ranks, ra
     ms = max_over_ranks(start.elapsed_time(end)) / iters
     result = {"heads_per_gpu": heads, "ms": ms, "states_per_s": world * heads / (ms / 1e3),
               "bit_exact_to": "FromDenseBoundary (tests/test_gpu_full.py)"}
-    if rank == 0:
-        result["cpu_reference"] = full_codec_cpu_reference()
+    result["cpu_reference"] = (full_codec_cpu_reference() if world == 1
+                               else {"skipped": CPU_AT_N1})
     return result
 
 
