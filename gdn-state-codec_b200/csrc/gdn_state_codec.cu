@@ -751,7 +751,7 @@ int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
     uint32_t states) {
   if (dense_state == nullptr || decay == nullptr || key == nullptr || read == nullptr ||
       query == nullptr || value == nullptr || output == nullptr || states == 0u ||
-      !gdnsc::aligned4(dense_state) || !gdnsc::aligned4(decay) || !gdnsc::aligned2(key) ||
+      !gdnsc::aligned16(dense_state) || !gdnsc::aligned4(decay) || !gdnsc::aligned2(key) ||
       !gdnsc::aligned2(read) || !gdnsc::aligned2(query) || !gdnsc::aligned2(value) ||
       !gdnsc::aligned4(output)) {
     return gdnsc::kBadArgs;

@@ -570,6 +570,12 @@ inline size_t window_fold_smem_bytes() {
 // 10-16), in place on capsule-layout [k][v] states: per value column v,
 // correction = value[v] - sum_k S[k][v] read[k]; S[k][v] = decay S[k][v] +
 // key[k] correction; out[v] = sum_k S_new[k][v] query[k] (k in order).
+//
+// HBM-bound (64 KiB read + 64 KiB written per head).  Persistent 128-thread
+// CTAs, three per SM, each with one 64 KiB landing buffer filled by a single
+// bulk copy: both column passes read the head from shared memory, so each
+// state element crosses HBM once each way.  Thread t owns value column t;
+// the updated rows go straight to global memory, 512 contiguous bytes per key.
 
 struct DenseStepParams {
   float* state;              // [heads][128][128] capsule layout, updated in place
@@ -582,30 +588,87 @@ struct DenseStepParams {
   uint64_t heads;
 };
 
-__global__ void __launch_bounds__(kWinThreads) dense_step_kernel(DenseStepParams p) {
-  __shared__ float key[kKeys], read[kKeys], query[kKeys];
+constexpr int kDenseStepBlocksPerSm = 3;
+
+struct __align__(128) DenseStepShared {
+  float stage[kElements];    // the head's state, [k][v]
+  float4 key[kKeys / 4];     // token vectors, four keys per entry
+  float4 read[kKeys / 4];
+  float4 query[kKeys / 4];
+  uint64_t full;             // the stage holds the current head
+};
+
+__device__ __forceinline__ void dense_step_issue(const DenseStepParams& p, DenseStepShared& sh,
+                                                 uint64_t head) {
+  fence_proxy_async();
+  mbar_expect_tx(&sh.full, kElements * sizeof(float));
+  bulk_load(sh.stage, p.state + head * kElements, kElements * sizeof(float), &sh.full,
+            evict_first_policy());
+}
+
+__global__ void __launch_bounds__(kWinThreads, kDenseStepBlocksPerSm)
+    dense_step_kernel(DenseStepParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  DenseStepShared& sh = *reinterpret_cast<DenseStepShared*>(smem_raw);
   const int t = threadIdx.x;
+  if (t == 0) {
+    mbar_init(&sh.full, 1);
+    fence_mbar_init();
+    dense_step_issue(p, sh, blockIdx.x);  // the grid never exceeds the head count
+  }
+  __syncthreads();
+  uint32_t parity = 0;
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
-    key[t] = half_to_float(__ldg(p.keys + head * kKeys + t));
-    read[t] = half_to_float(__ldg(p.reads + head * kKeys + t));
-    query[t] = half_to_float(__ldg(p.queries + head * kKeys + t));
+    // Token inputs while the state lands.
+    reinterpret_cast<float*>(sh.key)[t] = half_to_float(__ldg(p.keys + head * kKeys + t));
+    reinterpret_cast<float*>(sh.read)[t] = half_to_float(__ldg(p.reads + head * kKeys + t));
+    reinterpret_cast<float*>(sh.query)[t] = half_to_float(__ldg(p.queries + head * kKeys + t));
     const float value = half_to_float(__ldg(p.values + head * kValues + t));
     const float decay = __ldg(p.decay + head);
-    __syncthreads();
-    float* s = p.state + head * kElements + t;
+    const uint32_t phase = parity;
+    parity ^= 1u;
+    const bool landed = mbar_wait_bounded(&sh.full, phase);
+    if (__syncthreads_or(!landed)) {  // token vectors published; uniform result
+      // A bounded wait expired: report it, let the copy land (again bounded)
+      // so that it no longer targets this block, and stop.
+      if (t == 0) {
+        report(nullptr, kStatusWaitTimeout);
+        (void)mbar_wait_bounded(&sh.full, phase);
+      }
+      return;
+    }
+    const float* s = sh.stage + t;
     float projection = 0.0F;
-#pragma unroll 8
-    for (int k = 0; k < kKeys; ++k) projection = __fadd_rn(projection, __fmul_rn(s[k * kValues], read[k]));
+#pragma unroll 4
+    for (int k4 = 0; k4 < kKeys / 4; ++k4) {
+      const float4 r = sh.read[k4];
+      const float* col = s + 4 * k4 * kValues;
+      projection = __fadd_rn(projection, __fmul_rn(col[0], r.x));
+      projection = __fadd_rn(projection, __fmul_rn(col[kValues], r.y));
+      projection = __fadd_rn(projection, __fmul_rn(col[2 * kValues], r.z));
+      projection = __fadd_rn(projection, __fmul_rn(col[3 * kValues], r.w));
+    }
     const float correction = __fsub_rn(value, projection);
+    float* dst = p.state + head * kElements + t;
     float out = 0.0F;
-#pragma unroll 8
-    for (int k = 0; k < kKeys; ++k) {
-      const float next = __fadd_rn(__fmul_rn(decay, s[k * kValues]), __fmul_rn(key[k], correction));
-      s[k * kValues] = next;
-      out = __fadd_rn(out, __fmul_rn(next, query[k]));
+#pragma unroll 2
+    for (int k4 = 0; k4 < kKeys / 4; ++k4) {
+      const float4 kk = sh.key[k4], qq = sh.query[k4];
+      const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
+      const float qv[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = 4 * k4 + i;
+        const float next = __fadd_rn(__fmul_rn(decay, s[k * kValues]),
+                                     __fmul_rn(kv[i], correction));
+        dst[k * kValues] = next;
+        out = __fadd_rn(out, __fmul_rn(next, qv[i]));
+      }
     }
     p.outputs[head * kValues + t] = out;
-    __syncthreads();
+    __syncthreads();  // every thread is done with the stage and the token vectors
+    const uint64_t next_head = head + gridDim.x;
+    if (t == 0 && next_head < p.heads) dense_step_issue(p, sh, next_head);
   }
 }
 
@@ -644,7 +707,11 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense, window_dense_kernel,
                                                       kDenseThreads, 0);
   if (err != cudaSuccess) return err;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->dense, dense_step_kernel, kWinThreads, 0);
+  err = cudaFuncSetAttribute(dense_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(DenseStepShared)));
+  if (err != cudaSuccess) return err;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->dense, dense_step_kernel, kWinThreads,
+                                                       sizeof(DenseStepShared));
 }
 
 inline cudaError_t launch_window_step(bool qwen, bool comp, const StepParams& p, int grid,
@@ -678,7 +745,7 @@ inline cudaError_t launch_window_dense(const FoldParams& p, int grid, cudaStream
 }
 
 inline cudaError_t launch_dense_step(const DenseStepParams& p, int grid, cudaStream_t stream) {
-  dense_step_kernel<<<grid, kWinThreads, 0, stream>>>(p);
+  dense_step_kernel<<<grid, kWinThreads, sizeof(DenseStepShared), stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -92,7 +92,8 @@ int32_t statecentric_gdn_state_codec_windowed_gdn_step_bf16_quant_only_launch_v1
 /* Dense fp32 GDN step (reference header :42-46), in place on [states][128]
  * [128] fp32 states in [key][value] order: correction = value - S^T read;
  * S = decay S + key (x) correction; output = S^T query.  key / read / query /
- * value binary16, decay fp32 [states], outputs fp32. */
+ * value binary16, decay fp32 [states], outputs fp32.  dense_state must be
+ * 16-byte aligned (each head is staged by one bulk copy); returns 1 otherwise. */
 int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
     void* stream, float* dense_state, const float* decay, const uint16_t* key,
     const uint16_t* read, const uint16_t* query, const uint16_t* value,
