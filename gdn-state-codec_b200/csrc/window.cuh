@@ -431,23 +431,27 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
 }
 
 // Quant-only refit (no power iterations): the window's DenseState streamed
-// straight to the workspace, one 256-thread CTA per head.  Thread t owns key
-// t mod 128 of every other pair of value rows (rows v, v + 1 with
-// v = 2 (t / 128) + 4 i), so each element pair of a thread shares its key's
-// record keys (held in registers as broadcast pairs) and reads the two rows'
-// record corrections as one adjacent pair from shared memory.  Every element
-// follows the reference order (dequantize, compensators by rank, records
-// oldest first) in packed fp32x2 arithmetic, each product rounded before its
-// add; a row's codes and its workspace row are read and written by 128
-// consecutive threads.
+// straight to the workspace, one 256-thread CTA per head.  Thread t owns the
+// key pair (2 (t mod 64), 2 (t mod 64) + 1) of rows v = t / 64 + 4 i, so an
+// element pair is adjacent in the provider layout [v][k]: its two codes are
+// one 16-bit word, its smoothing, record keys and compensator keys are natural
+// register pairs, and it is written with one 8-byte store.  The per-row
+// factors (scale, compensator values, record corrections) are the same for
+// both elements and for the whole warp (a warp holds one row), so shared
+// memory keeps them duplicated, (x, x), and one broadcast load yields the
+// packed operand.  Every element follows the reference order (dequantize,
+// compensators by rank, records oldest first) in packed fp32x2 arithmetic,
+// each product rounded before its add.
 constexpr int kDenseThreads = 256;
+constexpr int kDensePairs = kKeys / 2;                    // threads per row
+constexpr int kDenseRowGroups = kDenseThreads / kDensePairs;  // rows in flight per CTA
 
 struct __align__(16) WindowDenseShared {
-  int8_t codes[kElements];      // the head's codes, provider [v][k]
-  float rc[kWindow][kValues];   // record corrections
-  float cv[kRank][kValues];     // compensator values, transposed
-  float b[kValues];             // scales
-  f2 dd[kWindow];               // (decay, decay) per record
+  int8_t codes[kElements];              // the head's codes, provider [v][k]
+  float4 rc[kWindow / 2][kValues];      // (rc_u, rc_u, rc_u+1, rc_u+1) per row, u even
+  float4 cv[2][kValues];                // (V0, V0, V1, V1), (V2, V2, V3, V3) per row
+  f2 b[kValues];                        // (b, b) per row
+  float4 dd[kWindow / 2];               // (d_u, d_u, d_u+1, d_u+1), u even
 };
 
 // a / 127 for both lanes, exact for every float (the two-term reciprocal
@@ -459,11 +463,14 @@ __device__ __forceinline__ f2 div127x2_any(f2 a) {
   return ok ? div127x2(a) : pack2(div127_any(lo), div127_any(hi));
 }
 
+__device__ __forceinline__ f2 lo_pair(float4 v) { return pack2(v.x, v.y); }
+__device__ __forceinline__ f2 hi_pair(float4 v) { return pack2(v.z, v.w); }
+
 __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldParams p) {
   __shared__ WindowDenseShared sh;
   const int t = threadIdx.x;
-  const int k = t & (kKeys - 1);
-  const int group = t >> 7;
+  const int kp = t % kDensePairs;          // keys 2 kp, 2 kp + 1
+  const int row0 = t / kDensePairs;        // rows row0 + 4 i
   const bool comp = p.w.ck != nullptr;
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
     const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
@@ -481,44 +488,46 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
     // correction): v -> RN(1 v) + RN(0 0) = v, except that a -0 may become +0,
     // which the INT8 stage maps to the same codes, smoothing and scales.  The
     // record loop below is then free of position tests.
-    for (int i = t; i < kWindow * kValues; i += kDenseThreads) {
-      (&sh.rc[0][0])[i] = i < np * kValues
-                              ? half_to_float(__ldcg(p.w.record_corrections + rbase * kValues + i))
-                              : 0.0F;
+    for (int i = t; i < (kWindow / 2) * kValues; i += kDenseThreads) {
+      const int u = 2 * (i / kValues), v = i % kValues;
+      const uint16_t* rcs = p.w.record_corrections + rbase * kValues + v;
+      const float a = u < np ? half_to_float(__ldcg(rcs + u * kValues)) : 0.0F;
+      const float c = u + 1 < np ? half_to_float(__ldcg(rcs + (u + 1) * kValues)) : 0.0F;
+      sh.rc[u / 2][v] = make_float4(a, a, c, c);
     }
     if (t < kValues) {
-      sh.b[t] = __ldg(p.w.scales + head * kValues + t);
+      const float b = __ldg(p.w.scales + head * kValues + t);
+      sh.b[t] = pack2(b, b);
       if (comp) {
         const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
-        sh.cv[0][t] = half_to_float(vw.x & 0xFFFFu);
-        sh.cv[1][t] = half_to_float(vw.x >> 16);
-        sh.cv[2][t] = half_to_float(vw.y & 0xFFFFu);
-        sh.cv[3][t] = half_to_float(vw.y >> 16);
+        const float v0 = half_to_float(vw.x & 0xFFFFu), v1 = half_to_float(vw.x >> 16);
+        const float v2 = half_to_float(vw.y & 0xFFFFu), v3 = half_to_float(vw.y >> 16);
+        sh.cv[0][t] = make_float4(v0, v0, v1, v1);
+        sh.cv[1][t] = make_float4(v2, v2, v3, v3);
       }
     }
-    if (t < kWindow) {
-      const float d = t < np ? __ldcg(p.w.record_decay + rbase + t) : 1.0F;
-      sh.dd[t] = pack2(d, d);
+    if (t < kWindow / 2) {
+      const float d0 = 2 * t < np ? __ldcg(p.w.record_decay + rbase + 2 * t) : 1.0F;
+      const float d1 = 2 * t + 1 < np ? __ldcg(p.w.record_decay + rbase + 2 * t + 1) : 1.0F;
+      sh.dd[t] = make_float4(d0, d0, d1, d1);
     }
-    f2 rk[kWindow];
+    f2 rk[kWindow];  // (key 2 kp, key 2 kp + 1) of every record
 #pragma unroll
     for (int u = 0; u < kWindow; ++u) {
-      float r = 0.0F;
-      if (u < np) r = half_to_float(__ldcg(p.w.record_keys + (rbase + u) * kKeys + k));
-      rk[u] = pack2(r, r);
+      uint32_t w = 0u;
+      if (u < np) w = __ldcg(reinterpret_cast<const uint32_t*>(p.w.record_keys + (rbase + u) * kKeys) + kp);
+      rk[u] = pack2(half_to_float(w & 0xFFFFu), half_to_float(w >> 16));
     }
     f2 ck[kRank] = {0ull, 0ull, 0ull, 0ull};
     if (comp) {
-      const uint2 w = __ldg(reinterpret_cast<const uint2*>(p.w.ck + (head * kKeys + k) * kRank));
-      const float c0 = half_to_float(w.x & 0xFFFFu), c1 = half_to_float(w.x >> 16);
-      const float c2 = half_to_float(w.y & 0xFFFFu), c3 = half_to_float(w.y >> 16);
-      ck[0] = pack2(c0, c0);
-      ck[1] = pack2(c1, c1);
-      ck[2] = pack2(c2, c2);
-      ck[3] = pack2(c3, c3);
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.w.ck + head * kKeys * kRank) + kp);
+      // keys 2 kp (ranks 0..3 in w.x, w.y) and 2 kp + 1 (w.z, w.w)
+      ck[0] = pack2(half_to_float(w.x & 0xFFFFu), half_to_float(w.z & 0xFFFFu));
+      ck[1] = pack2(half_to_float(w.x >> 16), half_to_float(w.z >> 16));
+      ck[2] = pack2(half_to_float(w.y & 0xFFFFu), half_to_float(w.w & 0xFFFFu));
+      ck[3] = pack2(half_to_float(w.y >> 16), half_to_float(w.w >> 16));
     }
-    const float ct = __ldg(p.w.smoothing + head * kKeys + k);
-    const f2 cc = pack2(ct, ct);
+    const f2 cc = *reinterpret_cast<const f2*>(p.w.smoothing + head * kKeys + 2 * kp);
     __syncthreads();
     // ---- the window is about to be folded: clear it --------------------------
     for (int i = t; i < kWindow * kKeys; i += kDenseThreads) {
@@ -531,30 +540,32 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
       reinterpret_cast<uint2*>(p.next_ck + (head * kKeys + t) * kRank)[0] = make_uint2(0u, 0u);
       reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
     }
-    // ---- dense rows, two at a time -------------------------------------------
-    const int8_t* codes = sh.codes + k;  // provider [v][k]
-    float* out = p.workspace + head * kElements + k;
+    // ---- dense rows ----------------------------------------------------------
+    const uint16_t* codes = reinterpret_cast<const uint16_t*>(sh.codes) + kp;  // [v][pair]
+    f2* out = reinterpret_cast<f2*>(p.workspace + head * kElements) + kp;
+    const f2 magic = pack2(kCodeMagic, kCodeMagic);
     bool finite = true;
 #pragma unroll 2
-    for (int i = 0; i < kValues / 4; ++i) {
-      const int v = 2 * group + 4 * i;
-      const f2 z = pack2(static_cast<float>(codes[v * kKeys]),
-                         static_cast<float>(codes[(v + 1) * kKeys]));
-      f2 val = mul2(div127x2_any(mul2(cc, z)), *reinterpret_cast<const f2*>(&sh.b[v]));
+    for (int i = 0; i < kValues / kDenseRowGroups; ++i) {
+      const int v = row0 + kDenseRowGroups * i;
+      const uint32_t biased = static_cast<uint32_t>(codes[v * kDensePairs]) ^ kCodeBias;
+      const f2 z = sub2(pack2(code_magic(biased, 0), code_magic(biased, 1)), magic);
+      f2 val = mul2(div127x2_any(mul2(cc, z)), sh.b[v]);
       if (comp) {
-#pragma unroll
-        for (int m = 0; m < kRank; ++m) {
-          val = add2(val, mul2_for_add(ck[m], *reinterpret_cast<const f2*>(&sh.cv[m][v])));
-        }
+        const float4 c01 = sh.cv[0][v], c23 = sh.cv[1][v];
+        val = add2(val, mul2_for_add(ck[0], lo_pair(c01)));
+        val = add2(val, mul2_for_add(ck[1], hi_pair(c01)));
+        val = add2(val, mul2_for_add(ck[2], lo_pair(c23)));
+        val = add2(val, mul2_for_add(ck[3], hi_pair(c23)));
       }
 #pragma unroll
-      for (int u = 0; u < kWindow; ++u) {
-        val = add2(mul2_for_add(sh.dd[u], val),
-                   mul2_for_add(rk[u], *reinterpret_cast<const f2*>(&sh.rc[u][v])));
+      for (int j = 0; j < kWindow / 2; ++j) {
+        const float4 d = sh.dd[j], r = sh.rc[j][v];
+        val = add2(mul2_for_add(lo_pair(d), val), mul2_for_add(rk[2 * j], lo_pair(r)));
+        val = add2(mul2_for_add(hi_pair(d), val), mul2_for_add(rk[2 * j + 1], hi_pair(r)));
       }
       finite = finite && isfinite(lo2(val)) && isfinite(hi2(val));
-      __stcg(out + v * kKeys, lo2(val));
-      __stcg(out + (v + 1) * kKeys, hi2(val));
+      __stcg(reinterpret_cast<unsigned long long*>(out + v * kDensePairs), val);
     }
     if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
   }
