@@ -466,6 +466,45 @@ __device__ __forceinline__ f2 div127x2_any(f2 a) {
 __device__ __forceinline__ f2 lo_pair(float4 v) { return pack2(v.x, v.y); }
 __device__ __forceinline__ f2 hi_pair(float4 v) { return pack2(v.z, v.w); }
 
+// The workspace rows of one thread (rows row0 + 4 i, keys 2 kp, 2 kp + 1).
+// Returns an accumulator that stays +0 while every element is finite and
+// becomes NaN otherwise (x * 0 is NaN exactly for infinite or NaN x).
+__device__ __forceinline__ f2 dense_rows(const WindowDenseShared& sh, f2 cc, bool c_safe,
+                                         const f2 (&rk)[kWindow], const f2 (&ck)[kRank],
+                                         bool comp, int row0, int kp, float* workspace) {
+  const uint16_t* codes = reinterpret_cast<const uint16_t*>(sh.codes) + kp;  // [v][pair]
+  f2* out = reinterpret_cast<f2*>(workspace) + kp;
+  const f2 magic = pack2(kCodeMagic, kCodeMagic);
+  const f2 zero = pack2(0.0F, 0.0F);
+  f2 flags = zero;
+#pragma unroll 2
+  for (int i = 0; i < kValues / kDenseRowGroups; ++i) {
+    const int v = row0 + kDenseRowGroups * i;
+    const uint32_t biased = static_cast<uint32_t>(codes[v * kDensePairs]) ^ kCodeBias;
+    const f2 z = sub2(pack2(code_magic(biased, 0), code_magic(biased, 1)), magic);
+    const f2 cz = mul2(cc, z);
+    f2 q = div127x2(cz);
+    if (!c_safe) q = div127x2_any(cz);  // a smoothing below 2^-112 in magnitude
+    f2 val = mul2(q, sh.b[v]);
+    if (comp) {
+      const float4 c01 = sh.cv[0][v], c23 = sh.cv[1][v];
+      val = add2(val, mul2_for_add(ck[0], lo_pair(c01)));
+      val = add2(val, mul2_for_add(ck[1], hi_pair(c01)));
+      val = add2(val, mul2_for_add(ck[2], lo_pair(c23)));
+      val = add2(val, mul2_for_add(ck[3], hi_pair(c23)));
+    }
+#pragma unroll
+    for (int j = 0; j < kWindow / 2; ++j) {
+      const float4 d = sh.dd[j], r = sh.rc[j][v];
+      val = add2(mul2_for_add(lo_pair(d), val), mul2_for_add(rk[2 * j], lo_pair(r)));
+      val = add2(mul2_for_add(hi_pair(d), val), mul2_for_add(rk[2 * j + 1], hi_pair(r)));
+    }
+    flags = fma2(val, zero, flags);
+    __stcg(reinterpret_cast<unsigned long long*>(out + v * kDensePairs), val);
+  }
+  return flags;
+}
+
 __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldParams p) {
   __shared__ WindowDenseShared sh;
   const int t = threadIdx.x;
@@ -541,32 +580,16 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
       reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
     }
     // ---- dense rows ----------------------------------------------------------
-    const uint16_t* codes = reinterpret_cast<const uint16_t*>(sh.codes) + kp;  // [v][pair]
-    f2* out = reinterpret_cast<f2*>(p.workspace + head * kElements) + kp;
-    const f2 magic = pack2(kCodeMagic, kCodeMagic);
-    bool finite = true;
-#pragma unroll 2
-    for (int i = 0; i < kValues / kDenseRowGroups; ++i) {
-      const int v = row0 + kDenseRowGroups * i;
-      const uint32_t biased = static_cast<uint32_t>(codes[v * kDensePairs]) ^ kCodeBias;
-      const f2 z = sub2(pack2(code_magic(biased, 0), code_magic(biased, 1)), magic);
-      f2 val = mul2(div127x2_any(mul2(cc, z)), sh.b[v]);
-      if (comp) {
-        const float4 c01 = sh.cv[0][v], c23 = sh.cv[1][v];
-        val = add2(val, mul2_for_add(ck[0], lo_pair(c01)));
-        val = add2(val, mul2_for_add(ck[1], hi_pair(c01)));
-        val = add2(val, mul2_for_add(ck[2], lo_pair(c23)));
-        val = add2(val, mul2_for_add(ck[3], hi_pair(c23)));
-      }
-#pragma unroll
-      for (int j = 0; j < kWindow / 2; ++j) {
-        const float4 d = sh.dd[j], r = sh.rc[j][v];
-        val = add2(mul2_for_add(lo_pair(d), val), mul2_for_add(rk[2 * j], lo_pair(r)));
-        val = add2(mul2_for_add(hi_pair(d), val), mul2_for_add(rk[2 * j + 1], hi_pair(r)));
-      }
-      finite = finite && isfinite(lo2(val)) && isfinite(hi2(val));
-      __stcg(reinterpret_cast<unsigned long long*>(out + v * kDensePairs), val);
-    }
+    // With this thread's smoothing pair at least 2^-112 in magnitude, zero or
+    // not finite, every product c z is zero or at least 2^-112 in magnitude
+    // (codes are integers), where the two-term reciprocal division is exact;
+    // otherwise each product is checked.
+    const float c0 = lo2(cc), c1 = hi2(cc);
+    const bool c_safe = (fabsf(c0) >= kDiv127Safe || c0 == 0.0F || c0 != c0) &&
+                        (fabsf(c1) >= kDiv127Safe || c1 == 0.0F || c1 != c1);
+    float* rows = p.workspace + head * kElements;
+    const f2 flags = dense_rows(sh, cc, c_safe, rk, ck, comp, row0, kp, rows);
+    const bool finite = lo2(flags) == 0.0F && hi2(flags) == 0.0F;
     if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
   }
 }
