@@ -469,9 +469,10 @@ __device__ __forceinline__ f2 hi_pair(float4 v) { return pack2(v.z, v.w); }
 // The workspace rows of one thread (rows row0 + 4 i, keys 2 kp, 2 kp + 1).
 // Returns an accumulator that stays +0 while every element is finite and
 // becomes NaN otherwise (x * 0 is NaN exactly for infinite or NaN x).
+template <bool kComp>
 __device__ __forceinline__ f2 dense_rows(const WindowDenseShared& sh, f2 cc, bool c_safe,
                                          const f2 (&rk)[kWindow], const f2 (&ck)[kRank],
-                                         bool comp, int row0, int kp, float* workspace) {
+                                         int row0, int kp, float* workspace) {
   const uint16_t* codes = reinterpret_cast<const uint16_t*>(sh.codes) + kp;  // [v][pair]
   f2* out = reinterpret_cast<f2*>(workspace) + kp;
   const f2 magic = pack2(kCodeMagic, kCodeMagic);
@@ -485,8 +486,11 @@ __device__ __forceinline__ f2 dense_rows(const WindowDenseShared& sh, f2 cc, boo
     const f2 cz = mul2(cc, z);
     f2 q = div127x2(cz);
     if (!c_safe) q = div127x2_any(cz);  // a smoothing below 2^-112 in magnitude
-    f2 val = mul2(q, sh.b[v]);
-    if (comp) {
+    // Rounded before the compensator adds: a single-use mul.f32x2 feeding an
+    // add.f32x2 would be contracted into one fma.  The +0 addend can turn a
+    // -0 product into +0, which the INT8 stage encodes identically.
+    f2 val = mul2_for_add(q, sh.b[v]);
+    if constexpr (kComp) {
       const float4 c01 = sh.cv[0][v], c23 = sh.cv[1][v];
       val = add2(val, mul2_for_add(ck[0], lo_pair(c01)));
       val = add2(val, mul2_for_add(ck[1], hi_pair(c01)));
@@ -505,12 +509,12 @@ __device__ __forceinline__ f2 dense_rows(const WindowDenseShared& sh, f2 cc, boo
   return flags;
 }
 
+template <bool kComp>
 __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldParams p) {
   __shared__ WindowDenseShared sh;
   const int t = threadIdx.x;
   const int kp = t % kDensePairs;          // keys 2 kp, 2 kp + 1
   const int row0 = t / kDensePairs;        // rows row0 + 4 i
-  const bool comp = p.w.ck != nullptr;
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
     const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
     const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
@@ -537,7 +541,7 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
     if (t < kValues) {
       const float b = __ldg(p.w.scales + head * kValues + t);
       sh.b[t] = pack2(b, b);
-      if (comp) {
+      if constexpr (kComp) {
         const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
         const float v0 = half_to_float(vw.x & 0xFFFFu), v1 = half_to_float(vw.x >> 16);
         const float v2 = half_to_float(vw.y & 0xFFFFu), v3 = half_to_float(vw.y >> 16);
@@ -558,7 +562,7 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
       rk[u] = pack2(half_to_float(w & 0xFFFFu), half_to_float(w >> 16));
     }
     f2 ck[kRank] = {0ull, 0ull, 0ull, 0ull};
-    if (comp) {
+    if constexpr (kComp) {
       const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.w.ck + head * kKeys * kRank) + kp);
       // keys 2 kp (ranks 0..3 in w.x, w.y) and 2 kp + 1 (w.z, w.w)
       ck[0] = pack2(half_to_float(w.x & 0xFFFFu), half_to_float(w.z & 0xFFFFu));
@@ -588,7 +592,7 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
     const bool c_safe = (fabsf(c0) >= kDiv127Safe || c0 == 0.0F || c0 != c0) &&
                         (fabsf(c1) >= kDiv127Safe || c1 == 0.0F || c1 != c1);
     float* rows = p.workspace + head * kElements;
-    const f2 flags = dense_rows(sh, cc, c_safe, rk, ck, comp, row0, kp, rows);
+    const f2 flags = dense_rows<kComp>(sh, cc, c_safe, rk, ck, row0, kp, rows);
     const bool finite = lo2(flags) == 0.0F && hi2(flags) == 0.0F;
     if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
   }
@@ -738,7 +742,7 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->fold, window_fold_kernel, kFitThreads,
                                                       window_fold_smem_bytes());
   if (err != cudaSuccess) return err;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense, window_dense_kernel,
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense, window_dense_kernel<true>,
                                                       kDenseThreads, 0);
   if (err != cudaSuccess) return err;
   err = cudaFuncSetAttribute(dense_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -774,7 +778,11 @@ inline cudaError_t launch_window_fold(const FoldParams& p, int grid, cudaStream_
 }
 
 inline cudaError_t launch_window_dense(const FoldParams& p, int grid, cudaStream_t stream) {
-  window_dense_kernel<<<grid, kDenseThreads, 0, stream>>>(p);
+  if (p.w.ck != nullptr) {
+    window_dense_kernel<true><<<grid, kDenseThreads, 0, stream>>>(p);
+  } else {
+    window_dense_kernel<false><<<grid, kDenseThreads, 0, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 
