@@ -225,6 +225,20 @@ def cpu_baseline(layout: str, target_seconds: float = 3.0) -> dict:
     }
 
 
+def arm_config(layout: str, world: int, slots: int = SLOTS) -> dict:
+    """The workload both arms report (the reference arm times a bounded
+    sample of it, described in its cpu_baseline.sample)."""
+    heads = slots * LAYERS * HEADS
+    name = "config2" if slots == SLOTS else f"config2 shape with {slots} slots"
+    return {
+        "workload": f"{name}: 30 GDN layers x {slots} slots x fp32 [32,128,128] per GPU, "
+                    "quantize (fused smoothing) + dequantize per step",
+        "layout": layout, "heads_per_gpu": heads, "global_batch": heads * world,
+        "parallelism": f"dp{world} (request slots sharded, no inter-GPU traffic)",
+        "l2": "inputs larger than L2 (9.1 GB touched per step vs 126 MB L2)",
+    }
+
+
 def run_reference(args) -> None:
     """--impl reference: the reference's CPU codec path on all host cores,
     each step a bounded sample of the batched workload."""
@@ -251,8 +265,7 @@ def run_reference(args) -> None:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": elapsed / args.steps * 1e3, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 sample: quantize+dequantize, CPU", "layout": args.layout,
-                   "heads_per_step": sample_heads},
+        "config": arm_config(args.layout, args.gpus, args.slots),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -442,13 +455,7 @@ def main() -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded on device: N(0,1) x 10^(-3u) per head, "
                                     "1% zeros)",
-            "config": {
-                "workload": "config2: 30 GDN layers x 64 slots x fp32 [32,128,128] per GPU, "
-                            "quantize (fused smoothing) + dequantize per step",
-                "layout": layout, "heads_per_gpu": heads, "global_batch": heads * world,
-                "parallelism": f"dp{world} (request slots sharded, no inter-GPU traffic)",
-                "l2": "inputs larger than L2 (9.1 GB touched per step vs 126 MB L2)",
-            },
+            "config": arm_config(layout, world, slots),
             "hbm_gbs_per_gpu": step_gbs,
             "hbm_frac_per_gpu": step_gbs / peak,
             "kernels": {
