@@ -266,6 +266,26 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src,
       "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
+// Shared -> global bulk store of `bytes` (multiple of 16, both addresses
+// 16-byte aligned), tracked by the issuing thread's bulk groups.  Before the
+// source buffer is written again, that thread waits with bulk_wait_read<N>
+// until at most N of its committed groups still read shared memory; before
+// the block exits, bulk_wait_all.
+__device__ __forceinline__ void bulk_store(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+               "r"(smem_addr(smem_src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
