@@ -215,6 +215,8 @@ def test_windowed_decode_entry_points_validate():
     assert call("window_boundary_launch_v1", n, *boundary[:-1], m, 1, 0) == BAD_ARGS
     assert call("fp32_gdn_step_launch_v1", n, a, a, a, a, a, a, a, 0) == BAD_ARGS
     assert call("fp32_gdn_step_launch_v1", n, n, a, a, a, a, a, a, 1) == BAD_ARGS
+    # the dense state is staged by bulk copies: 16-byte alignment required
+    assert call("fp32_gdn_step_launch_v1", n, a + 4, a, a, a, a, a, a, 1) == BAD_ARGS
 
 
 def test_valid_arguments_without_a_device_report_setup_failure():
