@@ -358,7 +358,6 @@ __device__ __forceinline__ uint64_t get_u64(const uint8_t* p) {
   for (int i = 0; i < 8; ++i) v |= static_cast<uint64_t>(p[i]) << (8 * i);
   return v;
 }
-__device__ __forceinline__ float get_f32(const uint8_t* p) { return __uint_as_float(get_u32(p)); }
 
 // Restore, part 1 (thread per capsule): the header checks and the SHA-256
 // digest, which is sequential within a capsule -- checks 1 to 6 of

@@ -292,14 +292,10 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return policy;
 }
 
-// Streaming (evict-first) 128-bit / 32-bit global stores and loads.
-__device__ __forceinline__ void st_cs_v4(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+// Streaming (evict-first) 32-bit global store and load.
 __device__ __forceinline__ void st_cs_u32(void* p, uint32_t v) { __stcs(reinterpret_cast<unsigned int*>(p), v); }
 __device__ __forceinline__ uint32_t ld_cs_u32(const void* p) {
   return __ldcs(reinterpret_cast<const unsigned int*>(p));
-}
-__device__ __forceinline__ uint4 ld_cs_v4u(const void* p) {
-  return __ldcs(reinterpret_cast<const uint4*>(p));
 }
 
 // Asynchronous 16-byte global -> shared copies (cp.async, cached in L2 only),

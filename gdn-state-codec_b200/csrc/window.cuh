@@ -107,15 +107,8 @@ __device__ __forceinline__ uint16_t float_to_half_bits(float x) {
   return __half_as_ushort(__float2half_rn(x));
 }
 
-// One sequential dot product sum_k a[k * sa] * b[k * sb], k = 0..127.
-__device__ __forceinline__ float chain_dot(const float* a, int sa, const float* b, int sb) {
-  float acc = 0.0F;
-#pragma unroll 8
-  for (int k = 0; k < kKeys; ++k) acc = __fadd_rn(acc, __fmul_rn(a[k * sa], b[k * sb]));
-  return acc;
-}
-
-// The same for two contiguous, 16-byte aligned vectors, four keys per load.
+// One sequential dot product sum_k a[k] * b[k], k = 0..127, of two
+// contiguous, 16-byte aligned vectors, four keys per load.
 __device__ __forceinline__ float chain_dot4(const float* a, const float* b) {
   const float4* a4 = reinterpret_cast<const float4*>(a);
   const float4* b4 = reinterpret_cast<const float4*>(b);
