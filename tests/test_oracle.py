@@ -127,6 +127,23 @@ def test_two_stage_equals_fused():
         assert_same_bits("scales", b2, b)
 
 
+def test_sign_of_zero_does_not_reach_the_int8_stage():
+    """The window refit may turn a -0 of DenseState into +0 (its products are
+    formed as fma(a, b, +0)); quantizing either gives the same codes,
+    smoothing and scales, so the boundary it writes is unchanged."""
+    rng = np.random.default_rng(11)
+    state = rng.standard_normal((2, 128, 128)).astype(np.float32)
+    state[rng.random(state.shape) < 0.05] = 0.0
+    flipped = state.copy()
+    zeros = flipped == 0.0
+    flipped[zeros] = np.float32(-0.0)
+    assert np.signbit(flipped[zeros]).all() and not np.signbit(state[zeros]).any()
+    for layout in ("capsule", "provider"):
+        for got, want, what in zip(oracle.quantize(flipped, layout), oracle.quantize(state, layout),
+                                   ("codes", "smoothing", "scales")):
+            assert_same_bits(what, got, want)
+
+
 def test_quant_only_semantics_by_hand():
     """A head worked out by hand from capsule.cpp:190-225: zero columns give
     scale 0 and codes 0; the largest magnitude per value gets code +-127."""
