@@ -199,18 +199,29 @@ __host__ __device__ inline void sha256(const uint8_t* data, uint64_t size, uint3
 }
 
 // Device digest of `size` bytes at an 8-byte aligned `data`: whole blocks
-// are read as eight 8-byte words and byte-swapped to big-endian words.
+// are read as eight 8-byte words and byte-swapped to big-endian words.  The
+// next block's words are loaded while the current block is compressed, so
+// the load latency overlaps the 64 rounds.
 __device__ inline void sha256_aligned8(const uint8_t* data, uint64_t size, uint32_t h[8]) {
   sha256_init(h);
   uint32_t block[16];
   uint64_t done = 0;
+  uint2 next[8];
+  if (size >= 64) {
+    const uint2* words = reinterpret_cast<const uint2*>(data);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) next[i] = words[i];
+  }
   for (; done + 64 <= size; done += 64) {
-    const uint2* words = reinterpret_cast<const uint2*>(data + done);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint2 w = words[i];
-      block[2 * i] = __byte_perm(w.x, 0u, 0x0123);
-      block[2 * i + 1] = __byte_perm(w.y, 0u, 0x0123);
+      block[2 * i] = __byte_perm(next[i].x, 0u, 0x0123);
+      block[2 * i + 1] = __byte_perm(next[i].y, 0u, 0x0123);
+    }
+    if (done + 128 <= size) {
+      const uint2* words = reinterpret_cast<const uint2*>(data + done + 64);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) next[i] = words[i];
     }
     sha256_block(h, block);
   }
