@@ -267,3 +267,41 @@ def test_oracle_vs_reference_quant_only_stage():
         q = rng.standard_normal((states.shape[0], 128)).astype(np.float32)
         assert_same_bits("projection", oracle.project(z, c, b, q, threads=4),
                          oracle.ref_quant_project(rz, rc, rb, q, threads=4))
+
+
+@need_ref_quant
+def test_oracle_vs_reference_quant_only_property():
+    """Property check against the reference's own quant-only code over
+    generated heads: per-row and per-column magnitudes spread over up to 60
+    decades, sparse heads, signed zeros, exact dyadic values and repeated
+    magnitudes (rounding ties)."""
+    hypothesis = pytest.importorskip("hypothesis")
+    st = hypothesis.strategies
+
+    @hypothesis.settings(max_examples=40, deadline=None, derandomize=True)
+    @hypothesis.given(seed=st.integers(0, 2**32 - 1),
+                      row_decades=st.floats(0.0, 30.0), col_decades=st.floats(0.0, 30.0),
+                      zero_fraction=st.sampled_from([0.0, 0.01, 0.5, 0.99]),
+                      kind=st.sampled_from(["normal", "dyadic", "repeated"]),
+                      negative_zeros=st.booleans())
+    def check(seed, row_decades, col_decades, zero_fraction, kind, negative_zeros):
+        rng = np.random.default_rng(seed)
+        if kind == "normal":
+            head = rng.standard_normal((128, 128))
+        elif kind == "dyadic":
+            head = rng.integers(-255, 256, (128, 128)) * 2.0 ** -8
+        else:
+            head = rng.choice([-1.5, -0.75, 0.75, 1.5, 3.0], (128, 128))
+        head = head * 10.0 ** (row_decades * (rng.random((128, 1)) - 0.5))
+        head = head * 10.0 ** (col_decades * (rng.random((1, 128)) - 0.5))
+        head = head.astype(np.float32)
+        head[rng.random((128, 128)) < zero_fraction] = np.float32(-0.0 if negative_zeros else 0.0)
+        states = head[None]
+        z, c, b = oracle.quantize(states, "capsule")
+        rz, rc, rb = oracle.ref_quant_encode(states)
+        assert_same_bits("codes", z, rz)
+        assert_same_bits("smoothing", c, rc)
+        assert_same_bits("scales", b, rb)
+        assert_same_bits("dense", oracle.dequantize(z, c, b), oracle.ref_quant_decode(rz, rc, rb))
+
+    check()
