@@ -278,3 +278,48 @@ def test_random_compensators_bit_exact(batch):
         assert_close_and_exact(f"{layout} projection+comp", to_np(proj),
                                oracle.project(*args, to_np(q.float()), to_np(ck), to_np(cv),
                                               layout=layout))
+
+
+def _generated_heads(count: int, seed: int) -> np.ndarray:
+    """Heads over a grid of shapes: per-row and per-column magnitudes spread
+    over up to 60 decades, sparse heads, signed zeros, dyadic values and
+    repeated magnitudes (rounding ties)."""
+    rng = np.random.default_rng(seed)
+    heads = []
+    for i in range(count):
+        kind = ("normal", "dyadic", "repeated")[i % 3]
+        if kind == "normal":
+            head = rng.standard_normal((128, 128))
+        elif kind == "dyadic":
+            head = rng.integers(-255, 256, (128, 128)) * 2.0 ** -8
+        else:
+            head = rng.choice([-1.5, -0.75, 0.75, 1.5, 3.0], (128, 128))
+        row_decades, col_decades = rng.uniform(0.0, 30.0, 2)
+        head = head * 10.0 ** (row_decades * (rng.random((128, 1)) - 0.5))
+        head = head * 10.0 ** (col_decades * (rng.random((1, 128)) - 0.5))
+        head = head.astype(np.float32)
+        zero_fraction = (0.0, 0.01, 0.5, 0.99)[i % 4]
+        head[rng.random((128, 128)) < zero_fraction] = np.float32(-0.0 if i % 2 else 0.0)
+        heads.append(head)
+    return np.stack(heads)
+
+
+@pytest.mark.parametrize("layout", ["capsule", "provider"])
+def test_generated_heads_bit_exact(layout):
+    cap = _generated_heads(48, seed=31)
+    host = cap if layout == "capsule" else np.ascontiguousarray(cap.transpose(0, 2, 1))
+    states = torch.from_numpy(host).to(DEV)
+    enc = codec.quantize(states, layout)
+    dense = codec.dequantize(enc)
+    rng = np.random.default_rng(32)
+    q = torch.from_numpy(rng.standard_normal((host.shape[0], 128)).astype(np.float32)).to(DEV)
+    q = q.to(torch.bfloat16)
+    proj = codec.encoded_projection(enc, q)
+    torch.cuda.synchronize()
+    z, c, b = oracle.quantize(host, layout)
+    assert_bit_exact("generated smoothing", to_np(enc.smoothing), c)
+    assert_bit_exact("generated scales", to_np(enc.scales), b)
+    assert_bit_exact("generated codes", to_np(enc.codes), z)
+    assert_bit_exact("generated dense", to_np(dense), oracle.dequantize(z, c, b, layout=layout))
+    want = oracle.project(z, c, b, to_np(q.float()), layout=layout)
+    assert np.array_equal(to_np(proj), want, equal_nan=True)
