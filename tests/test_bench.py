@@ -52,3 +52,42 @@ def test_short_region_takes_the_next_sample_and_says_so():
 def test_unparseable_lines_are_ignored():
     sampler = _sampler([(2.0, "[N/A]"), (2.1, _line(1965))])
     assert sampler.stop(1.0, 3.0)["samples"] == 1
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` runs the reference's CPU codec (or the C
+    restatement where that library is absent) and prints one JSON line with
+    the device arm's metric, unit, config and the e2e / cpu_baseline objects."""
+    import json
+    import subprocess
+    import sys
+
+    result = subprocess.run([sys.executable, str(bench.ROOT / "bench.py"), "--impl", "reference",
+                             "--steps", "1", "--warmup", "1"],
+                            capture_output=True, text=True, timeout=300)
+    assert result.returncode == 0, result.stderr
+    lines = [line for line in result.stdout.splitlines() if line.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference"
+    assert line["metric"] == bench.METRIC and line["unit"] == bench.UNIT
+    assert line["higher_is_better"] is True and line["value"] > 0
+    assert line["config"] == bench.arm_config("capsule", 1)
+    assert line["cpu_baseline"]["kind"] in ("reference", "port")
+    assert line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": bench.UNIT,
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_prints_nothing_on_other_ranks():
+    """Under torchrun only rank 0 runs the CPU reference; other ranks exit 0."""
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    result = subprocess.run([sys.executable, str(bench.ROOT / "bench.py"), "--impl", "reference",
+                             "--gpus", "2", "--steps", "1", "--warmup", "1"],
+                            capture_output=True, text=True, timeout=300, env=env)
+    assert result.returncode == 0, result.stderr
+    assert not [line for line in result.stdout.splitlines() if line.startswith("{")]
