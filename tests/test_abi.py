@@ -229,3 +229,34 @@ def test_valid_arguments_without_a_device_report_setup_failure():
     assert call("initialize_launch_v3", None, a, a, a, a, 1) == 3
     assert call("provider_dequantize_launch_v2", None, a, a, a, None, None, a, 1) == 3
     assert call("windowed_gdn_step_bf16_launch_v1", None, *_window(), *([a] * 6), 2) == 3
+
+
+def test_headers_compile_as_c_and_link(tmp_path):
+    """A C caller (the reference's C ABI has no C++ types) includes both
+    headers, links the core library and gets 1 from a launcher given null
+    pointers, which validation refuses before any CUDA call."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    source = tmp_path / "caller.c"
+    source.write_text(
+        '#include "statecentric/gdn_state_codec_kernel.h"\n'
+        '#include "statecentric/gdn_state_codec_windowed_gdn_kernel.h"\n'
+        "int main(void) {\n"
+        "  int32_t status = statecentric_gdn_state_codec_provider_initialize_launch_v3(\n"
+        "      (void*)0, (const float*)0, (float*)0, (int8_t*)0, (float*)0, 1u);\n"
+        "  int32_t window = statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(\n"
+        "      (void*)0, (float*)0, (const float*)0, (const uint16_t*)0, (const uint16_t*)0,\n"
+        "      (const uint16_t*)0, (const uint16_t*)0, (float*)0, 1u);\n"
+        "  return status == 1 && window == 1 ? 0 : 1;\n"
+        "}\n")
+    lib_dir = Path(_native.DEFAULT_LIBRARY_DIR)
+    exe = tmp_path / "caller"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                    f"-I{ROOT / 'include'}", str(source), "-o", str(exe), f"-L{lib_dir}",
+                    f"-l:{_native.CORE_LIBRARY}", f"-Wl,-rpath,{lib_dir}"],
+                   check=True, capture_output=True, text=True)
+    assert subprocess.run([str(exe)], timeout=60).returncode == 0
