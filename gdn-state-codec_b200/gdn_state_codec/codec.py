@@ -536,6 +536,25 @@ def _window_args(window: WindowStates):
             _ptr(window.record_keys), _ptr(window.record_corrections), _ptr(window.positions))
 
 
+def _window_launch(window: WindowStates):
+    """(heads, pointer arguments) of a window's buffers, validated once per set
+    of buffers: a later call with the same tensor objects at the same
+    addresses reuses the result, so a decode loop pays for the checks of its
+    per-token inputs only."""
+    tensors = (window.encoded.codes, window.encoded.smoothing, window.encoded.scales,
+               window.compensator_keys, window.compensator_values, window.record_decay,
+               window.record_keys, window.record_corrections, window.positions)
+    addresses = tuple(0 if t is None else t.data_ptr() for t in tensors)
+    cached = window.__dict__.get("_launch")
+    if (cached is not None and cached[1] == addresses
+            and all(a is b for a, b in zip(cached[0], tensors))):
+        return cached[2], cached[3]
+    heads = _check_window(window)
+    launch = (heads, _window_args(window))
+    window.__dict__["_launch"] = (tensors, addresses, *launch)
+    return launch
+
+
 def _vectors(heads: int, device, dtype, shapes: dict) -> None:
     for name, (tensor, count) in shapes.items():
         if _check(tensor, name, dtype, (KEY_DIMENSION,), device) != count:
@@ -551,7 +570,7 @@ def window_step_bf16(window: WindowStates, log_decay: torch.Tensor, beta: torch.
     bf16 outputs [H, 128] and appends one record per head.  The boundary must
     be provider layout.  Quant-only windows (no compensators) use the
     quant-only kernel."""
-    heads = _check_window(window)
+    heads, window_args = _window_launch(window)
     device = window.encoded.codes.device
     if window.encoded.layout != "provider":
         raise ValueError("the bf16 decode step reads provider-layout boundaries")
@@ -571,7 +590,7 @@ def window_step_bf16(window: WindowStates, log_decay: torch.Tensor, beta: torch.
             else "windowed_gdn_step_bf16_launch_v1")
     with torch.cuda.device(device):
         _status("decode step", _native.call(
-            "statecentric_gdn_state_codec_" + name, _stream(device), *_window_args(window),
+            "statecentric_gdn_state_codec_" + name, _stream(device), *window_args,
             _ptr(log_decay), _ptr(beta), _ptr(keys), _ptr(queries), _ptr(values), _ptr(out),
             heads))
     return out

@@ -50,3 +50,27 @@ def test_capsule_status_names_cover_restore_checks():
     # Restore's checks in the reference's order (capsule.cpp:477-578), 0 = restored.
     assert sorted(codec.CAPSULE_STATUS) == list(range(10))
     assert codec.CAPSULE_BYTES == 21688
+
+
+def test_window_buffers_are_validated_once_per_set_of_buffers(monkeypatch):
+    calls = []
+    monkeypatch.setattr(codec, "_check_window", lambda w: calls.append("check") or 4)
+    monkeypatch.setattr(codec, "_window_args", lambda w: ("args",))
+
+    def tensor(*shape, dtype=torch.float32):
+        return torch.zeros(shape, dtype=dtype)
+
+    window = codec.WindowStates(
+        codec.EncodedStates(tensor(4, 128, 128, dtype=torch.int8), tensor(4, 128),
+                            tensor(4, 128), "provider"),
+        None, None, tensor(4, 16), tensor(4, 16, 128, dtype=torch.float16),
+        tensor(4, 16, 128, dtype=torch.float16), tensor(4, 8, dtype=torch.int32))
+    assert codec._window_launch(window) == (4, ("args",))
+    assert codec._window_launch(window) == (4, ("args",))
+    assert calls == ["check"]
+    window.positions = tensor(4, 8, dtype=torch.int32)  # a new buffer: checked again
+    codec._window_launch(window)
+    assert calls == ["check", "check"]
+    assert window == codec.WindowStates(window.encoded, None, None, window.record_decay,
+                                        window.record_keys, window.record_corrections,
+                                        window.positions)  # the cache is not a field
