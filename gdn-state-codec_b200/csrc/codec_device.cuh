@@ -244,13 +244,15 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: gives up after `limit_ns` and returns false.
+// Bounded wait: gives up after `limit_ns` (2 s unless a test-support launch
+// asks for less) and returns false.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
   }
   return true;
 }

@@ -105,10 +105,13 @@ int grid_for(uint64_t work_units, int sms, int blocks_per_sm) {
 
 int32_t run_quantize(void* stream, bool provider, int mode, const float* state,
                      const float* smoothing_in, float* smoothing, int8_t* codes, float* scales,
-                     uint64_t items, SlotMap map, uint32_t* status) {
+                     uint64_t items, SlotMap map, uint32_t* status,
+                     uint64_t wait_limit_ns = kWaitLimitNs, uint32_t arm_only = 0u) {
   const DeviceSetup* s = device_setup();
   if (s == nullptr) return kSetupFailed;
   QuantizeParams p{state, smoothing_in, smoothing, codes, scales, items, map, status};
+  p.wait_limit_ns = wait_limit_ns;
+  p.arm_only = arm_only;
   const uint64_t units = (items + quantize_units_per_block() - 1) / quantize_units_per_block();
   const int grid = grid_for(units, s->sms, s->quantize_blocks[provider][mode]);
   return launch_quantize(provider, mode, p, grid, static_cast<cudaStream_t>(stream)) ==
@@ -133,11 +136,14 @@ int32_t run_dequantize(void* stream, bool provider, const int8_t* codes, const f
 int32_t run_project(void* stream, bool provider, const int8_t* codes, const float* smoothing,
                     const float* scales, const float* ck, const float* cv,
                     const uint16_t* queries, float* outputs, uint64_t items, SlotMap map,
-                    uint32_t* status) {
+                    uint32_t* status, uint64_t wait_limit_ns = kWaitLimitNs,
+                    uint32_t arm_only = 0u) {
   const DeviceSetup* s = device_setup();
   if (s == nullptr) return kSetupFailed;
   const bool comp = ck != nullptr;
   ProjectParams p{codes, smoothing, scales, ck, cv, queries, outputs, items, map, status};
+  p.wait_limit_ns = wait_limit_ns;
+  p.arm_only = arm_only;
   const uint64_t blocks = (items + 3) / 4;  // four warps (heads) per block
   const int grid = grid_for(blocks, s->sms, s->project_blocks[provider][comp]);
   return launch_project(provider, p, grid, static_cast<cudaStream_t>(stream)) == cudaSuccess
@@ -601,6 +607,38 @@ int32_t statecentric_gdn_state_codec_division_selftest_v1(void* stream, const fl
   gdnsc::division_selftest_kernel<<<s->sms * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       numerators, divisors, quotients, count);
   return cudaGetLastError() == cudaSuccess ? gdnsc::kOk : gdnsc::kLaunchFailed;
+}
+
+// Test support: the capsule quantize and encoded projection with every
+// bounded wait made to run out (barriers armed, no copy issued).
+int32_t statecentric_gdn_state_codec_quantize_wait_selftest_v1(
+    void* stream, const float* residual, float* smoothing, int8_t* quantized, float* value_scales,
+    uint32_t states, uint64_t limit_ns, uint32_t* status) {
+  if (residual == nullptr || smoothing == nullptr || quantized == nullptr ||
+      value_scales == nullptr || status == nullptr || states == 0u || limit_ns == 0u ||
+      limit_ns > gdnsc::kWaitLimitNs || !aligned16(residual) || !aligned16(smoothing) ||
+      !aligned16(quantized) || !aligned16(value_scales)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_quantize(stream, false, gdnsc::kFused, residual, nullptr, smoothing,
+                             quantized, value_scales, states, SlotMap{nullptr, 1, 1}, status,
+                             limit_ns, 1u);
+}
+
+int32_t statecentric_gdn_state_codec_encoded_projection_wait_selftest_v1(
+    void* stream, const int8_t* residual, const float* smoothing, const float* scales,
+    const uint16_t* queries_bf16, float* outputs, uint32_t states, uint64_t limit_ns,
+    uint32_t* status) {
+  if (residual == nullptr || smoothing == nullptr || scales == nullptr ||
+      queries_bf16 == nullptr || outputs == nullptr || status == nullptr || states == 0u ||
+      limit_ns == 0u || limit_ns > gdnsc::kWaitLimitNs || !aligned16(residual) ||
+      !aligned16(smoothing) || !aligned16(scales) || !aligned16(outputs) ||
+      !gdnsc::aligned8(queries_bf16)) {
+    return gdnsc::kBadArgs;
+  }
+  return gdnsc::run_project(stream, false, residual, smoothing, scales, nullptr, nullptr,
+                            queries_bf16, outputs, states, SlotMap{nullptr, 1, 1}, status,
+                            limit_ns, 1u);
 }
 
 // ---- Windowed decode: step, boundary refit, dense fp32 step -------------------

@@ -13,9 +13,14 @@
 // x is the bf16 query widened to fp32 (exact).  Each warp owns one head and
 // each lane four outputs v = 4l..4l+3, so the sequential k-sum is four
 // independent fp32 chains per lane (two packed fp32x2 chains).
-//  * capsule codes [k][v]: at step k a warp reads one 128-byte code row;
-//    the loads of the next batch of 8 rows are in flight while the current
-//    batch is accumulated (software pipelining).
+//  * capsule codes [k][v]: every warp streams its heads' codes through its own
+//    two-stage shared-memory ring, 64 code rows (8 KiB) per stage, each stage
+//    filled by one bulk copy (cp.async.bulk, mbarrier completion, this GPU's
+//    own memory, no multicast).  While one half of a head is accumulated the
+//    other half is in flight, and the smoothing, query and scales of the next
+//    head are fetched one head ahead, so a warp never waits on a global load
+//    inside a head.  A lane reads its four codes of row k with one
+//    conflict-free 32-bit shared load.
 //  * provider codes [v][k]: a lane's four outputs are four code rows, so the
 //    warp loads its 16 KiB head with coalesced 128-bit loads, stores it to
 //    shared memory with an XOR swizzle on 16-byte chunks and reads its rows
@@ -28,7 +33,6 @@ namespace gdnsc {
 
 constexpr int kPThreads = 128;
 constexpr int kPWarps = kPThreads / 32;
-constexpr int kPBatch = 8;   // capsule code rows per pipelined batch
 
 struct ProjectParams {
   const int8_t* codes;              // [heads][128][128]
@@ -41,10 +45,30 @@ struct ProjectParams {
   uint64_t items;
   SlotMap map;
   uint32_t* status;
+  uint64_t wait_limit_ns = kWaitLimitNs;  // limit of every bounded wait
+  // Test support (encoded_projection_wait_selftest_v1, capsule codes): arm
+  // each ring stage with its bytes but issue no copy, so every wait runs out
+  // with nothing in flight.
+  uint32_t arm_only = 0u;
 };
 
+// Capsule codes: per-warp ring of kRingStages stages of kRingRows code rows.
+// A warp's positions t = 0, 1, 2, ... are (its item number t / kRingPerHead,
+// rows (t % kRingPerHead) * kRingRows ..); position t uses stage
+// t % kRingStages, whose mbarrier completes once per use (phase parity
+// (t / kRingStages) & 1).  Sized by A/B timing on B200 (61,440 heads):
+// 64 rows x 2 stages beat 32 x 2, 32 x 3, 64 x 3 and 128 x 2.
+constexpr int kRingRows = 64;
+constexpr int kRingStages = 2;
+constexpr int kRingPerHead = kKeys / kRingRows;
+constexpr uint32_t kRingBytes = kRingRows * kValues;  // int8 codes per stage
+struct __align__(128) ProjectWarpShared {
+  uint32_t ring[kRingStages][kRingBytes / 4];
+  float2 cx[kKeys];                 // (c_k, x_k) of the current head
+  uint64_t bar[kRingStages];
+};
 struct ProjectShared {
-  float2 cx[kPWarps][kKeys];        // (c_k, x_k) per warp
+  ProjectWarpShared warp[kPWarps];
   float4 kr[kPWarps][kKeys];        // compensator keys per warp (full format only)
 };
 
@@ -124,83 +148,152 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
   ProjectShared& sh = *reinterpret_cast<ProjectShared*>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  ProjectWarpShared& ws = sh.warp[warp];
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kPWarps;
-  for (uint64_t item = static_cast<uint64_t>(blockIdx.x) * kPWarps + warp; item < p.items;
-       item += stride) {
+  const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kPWarps + warp;
+  if (lane == 0) {
+    for (int s = 0; s < kRingStages; ++s) mbar_init(&ws.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const uint64_t policy = evict_first_policy();
+  auto head_of = [&](uint64_t item) -> int64_t {
     bool bad = false;
-    const int64_t head = resolve_item(p.map, item, &bad);
+    return item < p.items ? resolve_item(p.map, item, &bad) : -1;
+  };
+  auto item_of = [&](uint64_t t) { return first + (t / kRingPerHead) * stride; };
+  // Lane 0 issues position t (see ProjectWarpShared).  A skipped head (PAD
+  // or invalid id) arrives with zero bytes, so its stage completes the same
+  // phase without a copy and the consumer waits uniformly.
+  auto issue = [&](uint64_t t) {
+    const uint64_t item = item_of(t);
+    if (item >= p.items) return;
+    const int64_t head = head_of(item);
+    const int stage = static_cast<int>(t % kRingStages);
+    fence_proxy_async();  // the stage's previous reads precede the copy
+    if (head < 0) {
+      mbar_expect_tx(&ws.bar[stage], 0);
+    } else {
+      mbar_expect_tx(&ws.bar[stage], kRingBytes);
+      if (p.arm_only == 0u) bulk_load(ws.ring[stage],
+                p.codes + static_cast<uint64_t>(head) * kElements +
+                    static_cast<uint64_t>(t % kRingPerHead) * kRingBytes,
+                kRingBytes, &ws.bar[stage], policy);
+    }
+  };
+  if (lane == 0) {
+    for (int t = 0; t < kRingStages; ++t) issue(t);
+  }
+  uint64_t pos = 0;  // next position to consume
+  // A lane whose bounded wait expires stops computing and issuing; the warp
+  // agrees on the failure once per head (lanes stay converged until then).
+  bool failed = false;
+  int fail_part = kRingPerHead;  // first part of the head whose wait expired
+  // Smoothing, query and scales of the next item, fetched one head ahead.
+  float4 c_next = make_float4(0.F, 0.F, 0.F, 0.F), b_next = c_next;
+  uint2 q_next = make_uint2(0u, 0u);
+  auto fetch = [&](uint64_t item, int64_t head) {
+    if (head < 0) return;
+    c_next = __ldg(reinterpret_cast<const float4*>(p.smoothing + static_cast<uint64_t>(head) * kKeys) + lane);
+    b_next = __ldg(reinterpret_cast<const float4*>(p.scales + static_cast<uint64_t>(head) * kValues) + lane);
+    q_next = __ldg(reinterpret_cast<const uint2*>(p.queries + item * kKeys) + lane);
+  };
+  int64_t next_head = head_of(first);
+  fetch(first, next_head);
+  for (uint64_t item = first; item < p.items; item += stride) {
+    bool bad = false;
+    (void)resolve_item(p.map, item, &bad);
+    const int64_t head = next_head;
+    next_head = head_of(item + stride);
+    // The output address is formed here, ahead of the ring loop: forming it
+    // after the loop measured 12 % slower on B200.
     float* out = p.outputs + item * kValues + 4 * lane;
+    const float4 c4 = c_next;
+    const float4 x4 = bf16x4_to_float4(q_next);
+    const float4 b4 = b_next;
+    fetch(item + stride, next_head);
+    __syncwarp();  // the previous head's readers are done with cx / kr
+    reinterpret_cast<float4*>(ws.cx)[2 * lane] = make_float4(c4.x, x4.x, c4.y, x4.y);
+    reinterpret_cast<float4*>(ws.cx)[2 * lane + 1] = make_float4(c4.z, x4.z, c4.w, x4.w);
+    if (kCompensated && head >= 0) {
+      const float4* kp = reinterpret_cast<const float4*>(p.compensator_keys) +
+                         static_cast<uint64_t>(head) * kKeys;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sh.kr[warp][4 * lane + i] = __ldg(kp + 4 * lane + i);
+    }
+    __syncwarp();
+    f2 a01 = pack2(0.F, 0.F), a23 = a01, kp01 = a01, kp23 = a01;
+    const float4* cx2 = reinterpret_cast<const float4*>(ws.cx);  // rows k, k + 1
+#pragma unroll 1
+    for (int part = 0; part < kRingPerHead; ++part, ++pos) {
+      const int stage = static_cast<int>(pos % kRingStages);
+      const uint32_t parity = static_cast<uint32_t>((pos / kRingStages) & 1u);
+      if (!failed && !mbar_wait_bounded(&ws.bar[stage], parity, p.wait_limit_ns)) {
+        failed = true;
+        fail_part = part;
+      }
+      if (head >= 0 && !failed) {
+        const uint32_t* rows = ws.ring[stage] + lane;
+#pragma unroll
+        for (int r0 = 0; r0 < kRingRows; r0 += 8) {
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = rows[(r0 + i) * 32];
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const int k = part * kRingRows + r0 + i;
+            const float4 cc = cx2[k >> 1];
+            f2 z01, z23;
+            unpack_codes(w[i], z01, z23);
+            accumulate(a01, a23, z01, z23, cc.x, cc.y);
+            unpack_codes(w[i + 1], z01, z23);
+            accumulate(a01, a23, z01, z23, cc.z, cc.w);
+            if (kCompensated) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float4 kk = sh.kr[warp][k + h];
+                const float x = h == 0 ? cc.y : cc.w;
+                const f2 xx = pack2(x, x);
+                kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
+                kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();  // every lane is done with this stage
+      if (lane == 0 && !failed) issue(pos + kRingStages);
+    }
+    if (__any_sync(0xffffffffu, failed)) {
+      // A bounded wait expired.  Lane 0 reports it and lets every copy that
+      // may still be in flight land (again bounded) before the warp leaves,
+      // so that no bulk copy targets the block's shared memory after it
+      // exits: positions from the first one any lane gave up on up to those
+      // lane 0 issued.  Outputs of this launch are then unspecified.
+      const uint64_t head_pos = pos - kRingPerHead;
+      const uint64_t from = head_pos + static_cast<uint32_t>(
+                                           __reduce_min_sync(0xffffffffu, static_cast<uint32_t>(fail_part)));
+      if (lane == 0) {
+        report(p.status, kStatusWaitTimeout);
+        const uint64_t to = (failed ? head_pos + fail_part : pos) + kRingStages;
+        for (uint64_t t = from; t < to; ++t) {
+          if (item_of(t) >= p.items) break;
+          (void)mbar_wait_bounded(&ws.bar[t % kRingStages], static_cast<uint32_t>((t / kRingStages) & 1u),
+                                 p.wait_limit_ns);
+        }
+      }
+      return;
+    }
     if (head < 0) {
       if (bad && lane == 0) report(p.status, kStatusBadSlot);
       *reinterpret_cast<float4*>(out) = make_float4(0.F, 0.F, 0.F, 0.F);
       continue;
     }
-    const uint64_t hbase = static_cast<uint64_t>(head);
-    const int8_t* codes = p.codes + hbase * kElements;
-    // (c_k, x_k) and compensator keys for this head into this warp's slots.
-    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.smoothing + hbase * kKeys) + lane);
-    const float4 x4 = bf16x4_to_float4(
-        __ldg(reinterpret_cast<const uint2*>(p.queries + item * kKeys) + lane));
-    __syncwarp();  // previous head's readers are done with this warp's slots
-    reinterpret_cast<float4*>(sh.cx[warp])[2 * lane] = make_float4(c4.x, x4.x, c4.y, x4.y);
-    reinterpret_cast<float4*>(sh.cx[warp])[2 * lane + 1] = make_float4(c4.z, x4.z, c4.w, x4.w);
-    if (kCompensated) {
-      const float4* kp = reinterpret_cast<const float4*>(p.compensator_keys) + hbase * kKeys;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sh.kr[warp][4 * lane + i] = __ldg(kp + 4 * lane + i);
-    }
-    __syncwarp();
-
-    f2 a01 = pack2(0.F, 0.F), a23 = pack2(0.F, 0.F);
-    f2 kp01 = pack2(0.F, 0.F), kp23 = pack2(0.F, 0.F);
-    {
-      // Software-pipelined over batches of kPBatch code rows: the loads of the
-      // next batch are in flight while this batch is accumulated.
-      const uint32_t* cw = reinterpret_cast<const uint32_t*>(codes) + lane;
-      const float4* cx2 = reinterpret_cast<const float4*>(sh.cx[warp]);  // rows k, k + 1
-      auto rows = [&](const uint32_t (&w)[kPBatch], int k) {
-#pragma unroll
-        for (int i = 0; i < kPBatch; i += 2) {
-          const float4 cc = cx2[(k + i) >> 1];
-          f2 z01, z23;
-          unpack_codes(w[i], z01, z23);
-          accumulate(a01, a23, z01, z23, cc.x, cc.y);
-          unpack_codes(w[i + 1], z01, z23);
-          accumulate(a01, a23, z01, z23, cc.z, cc.w);
-          if (kCompensated) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float4 kk = sh.kr[warp][k + i + h];
-              const float x = h == 0 ? cc.y : cc.w;
-              const f2 xx = pack2(x, x);
-              kp01 = add2(kp01, mul2_for_add(pack2(kk.x, kk.y), xx));
-              kp23 = add2(kp23, mul2_for_add(pack2(kk.z, kk.w), xx));
-            }
-          }
-        }
-      };
-      uint32_t wa[kPBatch], wb[kPBatch];
-#pragma unroll
-      for (int i = 0; i < kPBatch; ++i) wa[i] = ld_cs_u32(cw + i * 32);
-#pragma unroll 1
-      for (int k0 = 0; k0 < kKeys; k0 += 2 * kPBatch) {
-#pragma unroll
-        for (int i = 0; i < kPBatch; ++i) wb[i] = ld_cs_u32(cw + (k0 + kPBatch + i) * 32);
-        rows(wa, k0);
-        if (k0 + 2 * kPBatch < kKeys) {
-#pragma unroll
-          for (int i = 0; i < kPBatch; ++i) wa[i] = ld_cs_u32(cw + (k0 + 2 * kPBatch + i) * 32);
-        }
-        rows(wb, k0 + kPBatch);
-      }
-    }
-    const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.scales + hbase * kValues) + lane);
     // Every lane holds all four rank projections p_r (identical chains).
     const float* vbase = kCompensated
-                             ? p.compensator_values + (hbase * kValues + 4 * lane) * kRank
+                             ? p.compensator_values + (static_cast<uint64_t>(head) * kValues + 4 * lane) * kRank
                              : nullptr;
-    const float4 o = finish_outputs(a01, a23, b4, kCompensated, kp01, kp23, vbase);
-    __stcs(reinterpret_cast<float4*>(out), o);
+    __stcs(reinterpret_cast<float4*>(out), finish_outputs(a01, a23, b4, kCompensated, kp01, kp23, vbase));
   }
 }
 
@@ -349,7 +442,7 @@ size_t project_smem_bytes(bool provider, bool compensated) {
   if (provider) {
     return compensated ? sizeof(ProviderProjectShared) : offsetof(ProviderProjectShared, kr);
   }
-  return compensated ? sizeof(ProjectShared) : offsetof(ProjectShared, kr);
+  return compensated ? sizeof(ProjectShared) : offsetof(ProjectShared, kr);  // kr last
 }
 
 template <bool kProvider, bool kCompensated>

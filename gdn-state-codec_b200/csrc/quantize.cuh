@@ -71,6 +71,11 @@ struct QuantizeParams {
   uint64_t items;             // work items (heads, or entries * heads_per_slot)
   SlotMap map;
   uint32_t* status;           // optional caller status word
+  uint64_t wait_limit_ns = kWaitLimitNs;  // limit of every bounded wait
+  // Test support (quantize_wait_selftest_v1): arm the landing barrier for
+  // the first head's bytes but issue no copy at all, so the first wait runs
+  // out with nothing in flight.
+  uint32_t arm_only = 0u;
 };
 
 // Shared state of one CTA.
@@ -172,6 +177,7 @@ __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t 
 __device__ __forceinline__ void issue_head(const QuantizeParams& p, QuantizeGroupShared& gs,
                                            int64_t head) {
   fence_proxy_async();
+  if (p.arm_only != 0u) return;  // test support: only the first head is armed
   mbar_expect_tx(&gs.full, kElements * sizeof(float));
   bulk_load(gs.stage, p.state + static_cast<uint64_t>(head) * kElements, kElements * sizeof(float),
             &gs.full, evict_first_policy());
@@ -636,10 +642,18 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
   // the head (B1, B2) order every other shared array between heads.
   int64_t head = -1;
   uint64_t item = next_item(p, first, step, &head, gtid == 0);
-  if (gtid == 0 && head >= 0) issue_head(p, gs, head);
+  if (gtid == 0 && head >= 0) {
+    if (p.arm_only != 0u) {
+      // Test support: the first head's barrier expects bytes that never
+      // come, so the first wait runs out; no further arrival is made on it.
+      mbar_expect_tx(&gs.full, kElements * sizeof(float));
+    } else {
+      issue_head(p, gs, head);
+    }
+  }
   uint32_t parity = 0;
   while (head >= 0) {
-    bool timed_out = !mbar_wait_bounded(&gs.full, parity);
+    bool timed_out = !mbar_wait_bounded(&gs.full, parity, p.wait_limit_ns);
     CapsuleTile ct;
     float4 pv[kWarpRows];
     if (kProvider) {
@@ -665,7 +679,7 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
       // issues the next head.
       if (lane == 0) mbar_arrive(&gs.empty);
       if (gtid == 0 && next_head >= 0) {
-        if (mbar_wait_bounded(&gs.empty, parity)) {
+        if (mbar_wait_bounded(&gs.empty, parity, p.wait_limit_ns)) {
           issue_head(p, gs, next_head);
           issued = true;
         } else {
@@ -701,7 +715,7 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
       // unspecified.
       if (gtid == 0) {
         report(p.status, kStatusWaitTimeout);
-        if (issued) (void)mbar_wait_bounded(&gs.full, parity);
+        if (issued) (void)mbar_wait_bounded(&gs.full, parity, p.wait_limit_ns);
       }
       return;
     }

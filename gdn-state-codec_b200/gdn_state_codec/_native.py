@@ -62,6 +62,9 @@ SIGNATURES: dict[str, list] = {
     "statecentric_gdn_state_codec_synthesize_queries_v1":
         [_vp, _vp, _u64, _u32, _u32, _u32, _u32],
     "statecentric_gdn_state_codec_division_selftest_v1": [_vp, _vp, _vp, _vp, _u64],
+    "statecentric_gdn_state_codec_quantize_wait_selftest_v1": [_vp] * 5 + [_u32, _u64, _vp],
+    "statecentric_gdn_state_codec_encoded_projection_wait_selftest_v1":
+        [_vp] * 6 + [_u32, _u64, _vp],
     # windowed decode (gdn_state_codec_windowed_gdn_kernel.h)
     "statecentric_gdn_state_codec_windowed_gdn_step_launch_v1": [_vp] * 16 + [_u32],
     "statecentric_gdn_state_codec_windowed_gdn_step_bf16_launch_v1": [_vp] * 16 + [_u32],

@@ -269,6 +269,23 @@ int32_t statecentric_gdn_state_codec_division_selftest_v1(
     void* stream, const float* numerators, const float* divisors, float* quotients,
     uint64_t count);
 
+/* Test support for the failure path (no counterpart in the reference, which
+ * has no bounded device waits): the batched capsule-layout quantize
+ * (initialize_launch_v3) and encoded projection (encoded_projection_launch_v1,
+ * quant-only format) launched with their mbarriers armed for the bytes of a
+ * bulk copy that is never issued.  Every bounded wait therefore runs out after
+ * `limit_ns` nanoseconds (0 < limit_ns <= 2e9); the kernels OR bit 1 (value 2,
+ * "a bounded device wait expired") into *status (required) and into the sticky
+ * error word, and return.  No copy is in flight when they exit, so the CUDA
+ * context stays usable.  Outputs are unspecified. */
+int32_t statecentric_gdn_state_codec_quantize_wait_selftest_v1(
+    void* stream, const float* residual, float* smoothing, int8_t* quantized,
+    float* value_scales, uint32_t states, uint64_t limit_ns, uint32_t* status);
+int32_t statecentric_gdn_state_codec_encoded_projection_wait_selftest_v1(
+    void* stream, const int8_t* residual, const float* smoothing,
+    const float* scales, const uint16_t* queries_bf16, float* outputs,
+    uint32_t states, uint64_t limit_ns, uint32_t* status);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

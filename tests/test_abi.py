@@ -177,6 +177,23 @@ def test_status_and_support_entry_points_validate():
     assert call("division_selftest_v1", None, None, ALIGNED, ALIGNED, 1) == BAD_ARGS
 
 
+def test_wait_selftest_entry_points_validate():
+    """The failure-path test launchers refuse a missing status word, a zero
+    or over-long limit and the batched launchers' bad arguments."""
+    a, m, n = ALIGNED, MISALIGNED, None
+    q = "quantize_wait_selftest_v1"
+    assert call(q, n, a, a, a, a, 1, 1000, n) == BAD_ARGS           # no status word
+    assert call(q, n, a, a, a, a, 1, 0, a) == BAD_ARGS              # zero limit
+    assert call(q, n, a, a, a, a, 1, 2_000_000_001, a) == BAD_ARGS  # longer than 2 s
+    assert call(q, n, a, a, a, a, 0, 1000, a) == BAD_ARGS           # no states
+    assert call(q, n, m, a, a, a, 1, 1000, a) == BAD_ARGS           # misaligned state
+    p = "encoded_projection_wait_selftest_v1"
+    assert call(p, n, a, a, a, a, a, 1, 1000, n) == BAD_ARGS
+    assert call(p, n, a, a, a, a, a, 1, 0, a) == BAD_ARGS
+    assert call(p, n, a, a, a, n, a, 1, 1000, a) == BAD_ARGS        # no queries
+    assert call(p, n, a, a, a, a, a, 0, 1000, a) == BAD_ARGS
+
+
 def _window(a=ALIGNED):
     # codes, smoothing, scales, compensator keys / values, record decay /
     # keys / corrections, positions
