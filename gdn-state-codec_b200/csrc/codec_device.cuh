@@ -28,9 +28,13 @@ constexpr float kQuantMax = 127.0F;         // capsule.cpp:20
 constexpr float kSmoothingFloor = 1.0e-8F;  // capsule.h:17
 
 // Status bits a kernel ORs into the caller's status word (when one is given)
-// and into the library's sticky per-device error word.
-constexpr uint32_t kStatusBadSlot = 1u;      // slot id outside [-1, num_slots)
-constexpr uint32_t kStatusWaitTimeout = 2u;  // a bounded wait gave up
+// and into the library's sticky per-device error word.  Each condition has
+// its own bit.
+constexpr uint32_t kStatusBadSlot = 1u;          // bit 0: slot id outside [-1, num_slots)
+constexpr uint32_t kStatusWaitTimeout = 2u;      // bit 1: a bounded wait gave up
+constexpr uint32_t kStatusFitNonFinite = 4u;     // bit 2: full-codec fit saw non-finite data
+constexpr uint32_t kStatusWindowFull = 8u;       // bit 3: a decode step found a full window
+constexpr uint32_t kStatusWindowNonFinite = 16u; // bit 4: non-finite decode output or refit state
 
 // --------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (PTX ISA 8.6, sm_100a): two IEEE round-to-nearest

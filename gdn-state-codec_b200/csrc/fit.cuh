@@ -39,7 +39,6 @@ namespace gdnsc {
 constexpr int kFitThreads = 128;
 constexpr int kFitStride = 132;            // padded row of the shared residual
 constexpr int kFitIterations = 32;         // capsule.cpp:146
-constexpr uint32_t kStatusNonFinite = 4u;  // non-finite input or singular value
 
 // sinf((r + 1) (c + 1)) of the reference, computed on the host with the same
 // C library function (capsule.cpp:141-143) and uploaded once per device.
@@ -178,7 +177,7 @@ __device__ __forceinline__ void fit_ranks(FitShared& sh, int t, int iterations, 
         __syncthreads();
       }
       if (t == 0) {
-        if (!isfinite(sv)) report(status, kStatusNonFinite);
+        if (!isfinite(sv)) report(status, kStatusFitNonFinite);
         sh.norm = sv;
       }
     }
@@ -239,7 +238,7 @@ __global__ void __launch_bounds__(kFitThreads) fit_kernel(FitParams p) {
         sh.r[t][v] = x;
       }
     }
-    if (__syncthreads_or(!finite) != 0 && t == 0) report(p.status, kStatusNonFinite);
+    if (__syncthreads_or(!finite) != 0 && t == 0) report(p.status, kStatusFitNonFinite);
 
     fit_ranks<false>(sh, t, kFitIterations, head, p.compensator_keys, p.compensator_values,
                      p.status);

@@ -48,7 +48,6 @@ namespace gdnsc {
 constexpr int kWindow = 16;                 // capsule.h:14, p = 16
 constexpr int kPositionStride = 8;          // positions [head][8]
 constexpr int kWinThreads = 128;
-constexpr uint32_t kStatusWindowFull = 8u;  // a step found a head's window full
 constexpr float kQueryScale = 0.08838834764831845F;  // 128^-0.5 (windowed_gdn_step.cpp:297)
 
 struct WindowBuffers {
@@ -306,7 +305,7 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
     } else {
       static_cast<float*>(p.outputs)[head * kValues + t] = output;
     }
-    if (!isfinite(output)) report(nullptr, kStatusNonFinite);
+    if (!isfinite(output)) report(nullptr, kStatusWindowNonFinite);
     // ---- append the record -------------------------------------------------
     p.w.record_keys[(rbase + np) * kKeys + t] = float_to_half_bits(key_t);
     p.w.record_corrections[(rbase + np) * kValues + t] = float_to_half_bits(correction);
@@ -400,7 +399,7 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
       finite = finite && isfinite(value);
       sh.r[t][v] = value;
     }
-    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
+    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusWindowNonFinite);
     // ---- the window is folded: clear it (every read of it is done) ---------
 #pragma unroll 4
     for (int u = 0; u < kWindow; ++u) {
@@ -587,7 +586,7 @@ __global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldPara
     float* rows = p.workspace + head * kElements;
     const f2 flags = dense_rows<kComp>(sh, cc, c_safe, rk, ck, row0, kp, rows);
     const bool finite = lo2(flags) == 0.0F && hi2(flags) == 0.0F;
-    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusNonFinite);
+    if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusWindowNonFinite);
   }
 }
 

@@ -268,8 +268,9 @@ def full_encode(states: torch.Tensor, layout: str = "capsule", *,
                 status: torch.Tensor | None = None) -> FullEncoded:
     """FromDenseBoundary's encode (capsule.cpp:129-225) of every head: the
     rank-4 compensator fit, then smoothing + int8 quantize of the residual,
-    bit-identical to the portable C++ codec.  Non-finite data sets bit 2 of
-    ``status`` (int32 device scalar, optional) and of the device error word."""
+    bit-identical to the portable C++ codec.  Non-finite data sets
+    STATUS_FIT_NON_FINITE (bit 2, value 4) of ``status`` (int32 device
+    scalar, optional) and of the device error word."""
     heads = _check(states, "states", torch.float32, (KEY_DIMENSION, VALUE_DIMENSION))
     _heads_ok(heads)
     code = _layout(layout)
@@ -461,7 +462,6 @@ def encoded_projection_indexed(encoded_cache: EncodedStates, queries: torch.Tens
 
 WINDOW_SIZE = 16
 POSITION_STRIDE = 8
-STATUS_WINDOW_FULL = 8
 
 
 @dataclass
@@ -539,19 +539,22 @@ def _window_args(window: WindowStates):
 def _window_launch(window: WindowStates):
     """(heads, pointer arguments) of a window's buffers, validated once per set
     of buffers: a later call with the same tensor objects at the same
-    addresses reuses the result, so a decode loop pays for the checks of its
-    per-token inputs only."""
+    addresses, with the same dtype, shape and strides, reuses the result, so a
+    decode loop pays for the checks of its per-token inputs only.  An in-place
+    change of a buffer's metadata (resize_, transpose_, as_strided_, a new
+    .data) changes that key and triggers a new check."""
     tensors = (window.encoded.codes, window.encoded.smoothing, window.encoded.scales,
                window.compensator_keys, window.compensator_values, window.record_decay,
                window.record_keys, window.record_corrections, window.positions)
-    addresses = tuple(0 if t is None else t.data_ptr() for t in tensors)
+    key = tuple(None if t is None else (t.data_ptr(), t.dtype, t.shape, t.stride())
+                for t in tensors)
     cached = window.__dict__.get("_launch")
-    if (cached is not None and cached[1] == addresses
+    if (cached is not None and cached[1] == key
             and all(a is b for a, b in zip(cached[0], tensors))):
         return cached[2], cached[3]
     heads = _check_window(window)
     launch = (heads, _window_args(window))
-    window.__dict__["_launch"] = (tensors, addresses, *launch)
+    window.__dict__["_launch"] = (tensors, key, *launch)
     return launch
 
 
@@ -689,9 +692,18 @@ def dense_step(states: torch.Tensor, decay: torch.Tensor, keys: torch.Tensor,
 # ---------------------------------------------------------------------------
 # Status and synthetic inputs.
 
+# Bits of a caller's status word and of the sticky device error word.
+STATUS_BAD_SLOT = 1             # bit 0: a slot id outside [-1, num_slots) was skipped
+STATUS_WAIT_TIMEOUT = 2         # bit 1: a bounded device wait expired
+STATUS_FIT_NON_FINITE = 4       # bit 2: a full-codec fit saw non-finite data
+STATUS_WINDOW_FULL = 8          # bit 3: a decode step found a full window
+STATUS_WINDOW_NON_FINITE = 16   # bit 4: a decode output or refit state was non-finite
+
+
 def device_error(device: torch.device | str | int = "cuda", clear: bool = False) -> int:
-    """Sticky error bits of the device: 1 = invalid slot id, 2 = wait timeout,
-    4 = non-finite data in a full-codec fit."""
+    """Sticky error bits of the device (the STATUS_* values): 1 = invalid slot
+    id, 2 = wait timeout, 4 = non-finite data in a full-codec fit, 8 = decode
+    step on a full window, 16 = non-finite decode output or refit state."""
     bits = ctypes.c_uint32(0)
     with torch.cuda.device(device):
         _status("device error query", _native.call(

@@ -243,8 +243,11 @@ int32_t statecentric_gdn_state_codec_full_initialize_static_launch_v1(
 /* ---- Library status and benchmark support ------------------------------- */
 
 /* Read (and with clear != 0 reset) the sticky per-device error word of the
- * current device: bit 0 = an invalid slot id was seen, bit 1 = a bounded
- * device wait expired, bit 2 = non-finite data in a full-codec fit.
+ * current device, one bit per condition: bit 0 (value 1) = an invalid slot id
+ * was seen, bit 1 (value 2) = a bounded device wait expired, bit 2 (value 4)
+ * = non-finite data in a full-codec fit, bit 3 (value 8) = a decode step found
+ * a head's window full, bit 4 (value 16) = a decode output or refit state was
+ * non-finite.
  * Synchronous. */
 int32_t statecentric_gdn_state_codec_device_error_v1(uint32_t* bits, int32_t clear);
 

@@ -38,9 +38,9 @@
  * 16-byte aligned, a token vector not naturally aligned), 2 launch failed,
  * 3 device set-up failed.  `states` may be any value >= 1 (the Ascend launchers capped it at
  * 16384).  A step on a head whose window is already full (position 16)
- * leaves that head untouched and sets bit 8 of the sticky device error word
- * (statecentric_gdn_state_codec_device_error_v1); a non-finite output sets
- * bit 4.
+ * leaves that head untouched and sets bit 3 (value 8) of the sticky device
+ * error word (statecentric_gdn_state_codec_device_error_v1); a non-finite
+ * decode output or refit state sets bit 4 (value 16).
  */
 #ifndef STATECENTRIC_GDN_STATE_CODEC_WINDOWED_GDN_KERNEL_H_
 #define STATECENTRIC_GDN_STATE_CODEC_WINDOWED_GDN_KERNEL_H_

@@ -46,7 +46,8 @@ def build() -> None:
     import subprocess
 
     subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
-    ref_root = Path(os.environ.get("GDN_REFERENCE_ROOT", "/root/reference"))
+    # GDN_REFERENCE_ROOT when set, else a directory `reference` beside the repo.
+    ref_root = Path(os.environ.get("GDN_REFERENCE_ROOT", ORACLE_DIR.parent.parent / "reference"))
     if (ref_root / "native" / "src").is_dir():
         subprocess.run(
             ["make", "-s", "-C", str(ORACLE_DIR), "ref", f"REF={ref_root}"],

@@ -71,6 +71,19 @@ def test_window_buffers_are_validated_once_per_set_of_buffers(monkeypatch):
     window.positions = tensor(4, 8, dtype=torch.int32)  # a new buffer: checked again
     codec._window_launch(window)
     assert calls == ["check", "check"]
+    # In-place metadata changes keep the object and the address but change
+    # the shape or strides: each one is checked again.
+    window.record_decay.resize_(2, 16)  # smaller: same storage, same address
+    codec._window_launch(window)
+    assert calls == ["check"] * 3
+    window.encoded.smoothing.t_()
+    codec._window_launch(window)
+    assert calls == ["check"] * 4
+    window.encoded.scales.as_strided_((4, 64), (128, 1))
+    codec._window_launch(window)
+    assert calls == ["check"] * 5
+    codec._window_launch(window)  # unchanged since: cached
+    assert calls == ["check"] * 5
     assert window == codec.WindowStates(window.encoded, None, None, window.record_decay,
                                         window.record_keys, window.record_corrections,
                                         window.positions)  # the cache is not a field

@@ -90,5 +90,5 @@ def test_full_codec_reports_non_finite_input():
     codec.device_error(DEV, clear=True)
     codec.full_encode(dense, "capsule", status=status)
     torch.cuda.synchronize()
-    assert int(status.item()) & 4 == 4
-    assert codec.device_error(DEV, clear=True) & 4 == 4
+    assert int(status.item()) & codec.STATUS_FIT_NON_FINITE
+    assert codec.device_error(DEV, clear=True) & codec.STATUS_FIT_NON_FINITE

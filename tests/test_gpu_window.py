@@ -293,6 +293,8 @@ def test_non_finite_token_sets_the_status_bit():
                                  bf16_dev(inputs["beta"][0]), bf16_dev(inputs["keys"][0]),
                                  bf16_dev(inputs["queries"][0]), bf16_dev(values))
     torch.cuda.synchronize()
-    assert codec.device_error(DEV, clear=True) & 4
+    bits = codec.device_error(DEV, clear=True)
+    assert bits & codec.STATUS_WINDOW_NON_FINITE
+    assert not bits & codec.STATUS_FIT_NON_FINITE  # the fit's bit stays its own
     assert torch.isnan(out[1].float()).any()
     assert torch.isfinite(out[0].float()).all() and torch.isfinite(out[2:].float()).all()
