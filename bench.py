@@ -296,15 +296,17 @@ def main() -> None:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=device)
+        # Host-side plumbing only (barriers, max over ranks, the report): the
+        # codec's data path has no cross-GPU traffic, so no NCCL communicator
+        # is created.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 
     def barrier():
-        sharding.barrier()
         torch.cuda.synchronize(device)
+        sharding.barrier()
 
     def max_over_ranks(value: float) -> float:
-        return sharding.max_over_ranks(value, device=device)
+        return sharding.max_over_ranks(value)
 
     shard = sharding.weak_shard(rank, world, args.slots)
     slots = shard.count
@@ -559,7 +561,10 @@ def ragged_measure(codec, torch, layout, device, barrier, rank, world):
 def box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks, rank, world):
     """Config 5: 2,048 request slots x 30 layers x 32 heads partitioned by slot
     across the ranks (strong scaling, no inter-GPU traffic); one step =
-    quantize + encoded projection of every head of the rank's shard."""
+    quantize + encoded projection of every head of the rank's shard.  Each
+    rank also times its two kernels, so the report shows which rank's kernel
+    time sets the step, and checks a seeded sample of its heads against the
+    CPU oracle after the timed region."""
     shard = sharding.strong_shard(rank, world, 2048)
     per_slot = LAYERS * HEADS
     heads = shard.count * per_slot
@@ -578,22 +583,81 @@ def box_measure(codec, torch, sharding, layout, device, barrier, max_over_ranks,
     outputs = torch.empty(queries.shape, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
 
-    def step():
+    def step(events=None):
+        if events is not None:
+            events[0].record(stream)
         codec.quantize(states, layout, out=encoded)
+        if events is not None:
+            events[1].record(stream)
         codec.encoded_projection(encoded, queries, out=outputs)
+        if events is not None:
+            events[2].record(stream)
 
     for _ in range(3):
         step()
     barrier()
     iters = 10
-    ms = max_over_ranks(_timed(torch, stream, step, iters))
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(iters)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(iters):
+        step(events[i])
+    end.record(stream)
+    end.synchronize()
+    own_ms = start.elapsed_time(end) / iters
+    quant_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in events)
+    proj_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in events)
+    ms = max_over_ranks(own_ms)
+    per_rank = sharding.gather_over_ranks({"rank": rank, "slots": shard.count,
+                                           "ms_per_step": own_ms, "quantize_ms": quant_ms,
+                                           "projection_ms": proj_ms})
     barrier()
+    sample = box_parity_sample(codec, torch, layout, states, encoded, queries, outputs, rank)
+    mismatches = sharding.sum_over_ranks(sample["mismatches"])
     per_head = BYTES_PER_HEAD["quantize"] + BYTES_PER_HEAD["projection"]
     del states, encoded, queries, outputs
+    slowest = max(per_rank, key=lambda r: r["ms_per_step"])
     return {"slots": 2048, "slots_per_gpu": shard.count, "heads_per_gpu": heads,
             "scaling": "strong", "steps": iters, "ms_per_step": ms,
             "states_per_s": 2048 * per_slot / (ms / 1e3),
-            "hbm_gbs_per_gpu": per_head * heads / (ms / 1e3) / 1e9}
+            "hbm_gbs_per_gpu": per_head * heads / (ms / 1e3) / 1e9,
+            "per_rank": per_rank,
+            "limiter": (f"rank {slowest['rank']}'s own kernels: quantize "
+                        f"{slowest['quantize_ms']:.3f} ms + projection "
+                        f"{slowest['projection_ms']:.3f} ms of its {slowest['ms_per_step']:.3f} "
+                        f"ms step (max over ranks {ms:.3f} ms); no collective in the step"),
+            "parity_sampled_heads": sample["heads"] * world, "mismatches": int(mismatches),
+            "parity_checker": sample["checker"]}
+
+
+def box_parity_sample(codec, torch, layout, states, encoded, queries, outputs, rank,
+                      count: int = 512) -> dict:
+    """Check a seeded sample of the rank's heads (codes, smoothing, scales and
+    projection outputs) against the CPU oracle, outside the timed region."""
+    import numpy as np
+
+    import oracle  # the checker (oracle/), never the measured path
+
+    total = encoded.codes.numel() // (128 * 128)
+    rng = np.random.default_rng(1000 + rank)
+    pick = torch.as_tensor(np.sort(rng.choice(total, size=min(count, total), replace=False)),
+                           device=states.device)
+
+    def host(t, inner):
+        return t.reshape(total, *inner).index_select(0, pick).cpu().numpy()
+
+    z, c, b = (host(encoded.codes, (128, 128)), host(encoded.smoothing, (128,)),
+               host(encoded.scales, (128,)))
+    o = host(outputs, (128,))
+    q = host(queries.float(), (128,))
+    wz, wc, wb = oracle.quantize(host(states, (128, 128)), layout, threads=8)
+    wo = oracle.project(wz, wc, wb, q, layout=layout, threads=8)
+    bad = ~((z == wz).all(axis=(1, 2)) & (c.view(np.uint32) == wc.view(np.uint32)).all(axis=1)
+            & (b.view(np.uint32) == wb.view(np.uint32)).all(axis=1)
+            & (o.view(np.uint32) == wo.view(np.uint32)).all(axis=1))
+    return {"heads": int(pick.numel()), "mismatches": int(bad.sum()),
+            "checker": "oracle.quantize + oracle.project (CPU restatement pinned to the "
+                       "reference library) on seeded sampled heads, bit for bit"}
 
 
 # Algorithmic bytes of one decode step per head at window position p
@@ -936,14 +1000,51 @@ def committed_traffic(kernel: str, heads: int):
         return None
 
 
+def bind_host_to_gpu(torch, device) -> dict:
+    """Run this process on the host CPUs of the GPU's NUMA node (from sysfs),
+    so that pinned buffers allocated next are placed on that node by the
+    default first-touch policy.  Returns what was done; the caller restores
+    the previous CPU set afterwards."""
+    props = torch.cuda.get_device_properties(device)
+    bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    node_dir = Path("/sys/bus/pci/devices") / bus
+    info = {"pci": bus}
+    try:
+        info["numa_node"] = int((node_dir / "numa_node").read_text())
+        cpus = set()
+        for part in (node_dir / "local_cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            info["cpus"] = len(cpus)
+        else:
+            info["cpus"] = "unchanged (no overlap with the allowed CPUs)"
+    except (OSError, ValueError) as exc:
+        info["unbound"] = f"{type(exc).__name__}: {exc}"
+    return info
+
+
 def e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrier,
                 max_over_ranks, world):
     """Host fp32 states -> H2D -> quantize -> dequantize -> D2H fp32, per layer
-    chunk, with copies on their own streams so H2D, compute and D2H overlap."""
+    chunk, with copies on their own streams so H2D, compute and D2H overlap.
+    The pinned buffers are allocated on the GPU's NUMA node.  After the timed
+    region: the whole host output is compared with the device path, and each
+    rank's copy rates (H2D alone, D2H alone, both at once, all ranks at the
+    same time) are measured to name the host limit."""
+    from gdn_state_codec import sharding
+
+    saved_cpus = os.sched_getaffinity(0)
+    binding = bind_host_to_gpu(torch, device)
+    try:
+        host_in = torch.empty(states.shape, dtype=torch.float32, pin_memory=True)
+        host_in.copy_(states)
+        host_out = torch.empty_like(host_in, pin_memory=True)
+    finally:
+        os.sched_setaffinity(0, saved_cpus)
     chunk_heads = HEADS * slots  # one layer's worth of heads per chunk
-    host_in = torch.empty(states.shape, dtype=torch.float32, pin_memory=True)
-    host_in.copy_(states)
-    host_out = torch.empty_like(host_in, pin_memory=True)
     dev_in = torch.empty_like(states)
     dev_out = torch.empty_like(states)
     enc = codec.empty_encoded((slots, LAYERS, HEADS), layout, device)
@@ -993,14 +1094,54 @@ def e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrie
     torch.cuda.synchronize(device)
     barrier()
     ms = max_over_ranks(start.elapsed_time(end)) / steps
-    ok = bool(torch.equal(host_out[:1].to(device), codec.dequantize(
-        codec.quantize(states[:1].contiguous(), layout))))
+
+    # The whole host output against the device path (every head of the step).
+    codec.quantize(states, layout, out=enc)
+    codec.dequantize(enc, out=dev_out)
+    dev_in.copy_(host_out)
+    ok = bool(torch.equal(dev_in, dev_out))
+
     nbytes = states.numel() * 4
+
+    def copy_rate(copies) -> float:
+        """GB/s per direction of ``copies`` (stream, fn) run together, all
+        ranks at once."""
+        torch.cuda.synchronize(device)
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t0.record(compute)
+        for stream, _ in copies:
+            stream.wait_event(t0)
+        for stream, fn in copies:
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    fn()
+        for stream, _ in copies:
+            compute.wait_stream(stream)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t1.record(compute)
+        t1.synchronize()
+        return 2 * nbytes / (t0.elapsed_time(t1) / 1e3) / 1e9
+
+    up = (h2d, lambda: dev_in.copy_(host_in, non_blocking=True))
+    down = (d2h, lambda: host_out.copy_(dev_out, non_blocking=True))
+    rates = {"h2d_gbs": copy_rate([up]), "d2h_gbs": copy_rate([down]),
+             "both_gbs_each_way": copy_rate([up, down])}
+    per_rank = sharding.gather_over_ranks({"rank": torch.distributed.get_rank()
+                                           if world > 1 else 0, **binding, **rates})
+    slowest = min(r["both_gbs_each_way"] for r in per_rank)
+    copy_ms = nbytes / (slowest * 1e9) * 1e3
     return {"value": world * heads / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "steps": steps, "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
             "path": "gdn_state_codec.codec.quantize/dequantize (C ABI) per layer chunk, "
-                    "pinned host buffers, H2D/compute/D2H on separate streams",
-            "matches_device_path": ok}
+                    "pinned host buffers on the GPU's NUMA node, H2D/compute/D2H on "
+                    "separate streams",
+            "matches_device_path": ok, "matched_heads": heads,
+            "copy_rates_per_rank": per_rank,
+            "limiter": (f"host copies: a step moves {nbytes / 1e9:.2f} GB each way per rank; "
+                        f"with every rank copying both ways at once the slowest rank moves "
+                        f"{slowest:.1f} GB/s each way, {copy_ms:.1f} ms of the {ms:.1f} ms step "
+                        f"(the device kernels take about 2 ms)")}
 
 
 if __name__ == "__main__":

@@ -62,6 +62,9 @@ constexpr int kRingRows = 64;
 constexpr int kRingStages = 2;
 constexpr int kRingPerHead = kKeys / kRingRows;
 constexpr uint32_t kRingBytes = kRingRows * kValues;  // int8 codes per stage
+// With as many stages as parts per head, position t + kRingStages is the same
+// part of the warp's next item, whose head the warp has already resolved.
+static_assert(kRingStages == kRingPerHead, "the ring holds exactly one head");
 struct __align__(128) ProjectWarpShared {
   uint32_t ring[kRingStages][kRingBytes / 4];
   float2 cx[kKeys];                 // (c_k, x_k) of the current head
@@ -157,18 +160,18 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
   }
   __syncwarp();
   const uint64_t policy = evict_first_policy();
-  auto head_of = [&](uint64_t item) -> int64_t {
-    bool bad = false;
-    return item < p.items ? resolve_item(p.map, item, &bad) : -1;
+  // Head of an item (-1: padding, an invalid id (*bad) or past the end).
+  auto resolve = [&](uint64_t item, bool* bad) -> int64_t {
+    *bad = false;
+    return item < p.items ? resolve_item(p.map, item, bad) : -1;
   };
   auto item_of = [&](uint64_t t) { return first + (t / kRingPerHead) * stride; };
-  // Lane 0 issues position t (see ProjectWarpShared).  A skipped head (PAD
-  // or invalid id) arrives with zero bytes, so its stage completes the same
-  // phase without a copy and the consumer waits uniformly.
-  auto issue = [&](uint64_t t) {
-    const uint64_t item = item_of(t);
-    if (item >= p.items) return;
-    const int64_t head = head_of(item);
+  // Lane 0 issues position t of head `head` (see ProjectWarpShared).  A
+  // skipped head (PAD or invalid id) arrives with zero bytes, so its stage
+  // completes the same phase without a copy and the consumer waits
+  // uniformly; positions past the last item are not issued.
+  auto issue = [&](uint64_t t, int64_t head) {
+    if (item_of(t) >= p.items) return;
     const int stage = static_cast<int>(t % kRingStages);
     fence_proxy_async();  // the stage's previous reads precede the copy
     if (head < 0) {
@@ -181,8 +184,10 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
                 kRingBytes, &ws.bar[stage], policy);
     }
   };
+  bool next_bad = false;
+  int64_t next_head = resolve(first, &next_bad);
   if (lane == 0) {
-    for (int t = 0; t < kRingStages; ++t) issue(t);
+    for (int t = 0; t < kRingStages; ++t) issue(t, next_head);
   }
   uint64_t pos = 0;  // next position to consume
   // A lane whose bounded wait expires stops computing and issuing; the warp
@@ -198,13 +203,11 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
     b_next = __ldg(reinterpret_cast<const float4*>(p.scales + static_cast<uint64_t>(head) * kValues) + lane);
     q_next = __ldg(reinterpret_cast<const uint2*>(p.queries + item * kKeys) + lane);
   };
-  int64_t next_head = head_of(first);
   fetch(first, next_head);
   for (uint64_t item = first; item < p.items; item += stride) {
-    bool bad = false;
-    (void)resolve_item(p.map, item, &bad);
     const int64_t head = next_head;
-    next_head = head_of(item + stride);
+    const bool bad = next_bad;
+    next_head = resolve(item + stride, &next_bad);
     // The output address is formed here, ahead of the ring loop: forming it
     // after the loop measured 12 % slower on B200.
     float* out = p.outputs + item * kValues + 4 * lane;
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(kPThreads) project_kernel(ProjectParams p) {
         }
       }
       __syncwarp();  // every lane is done with this stage
-      if (lane == 0 && !failed) issue(pos + kRingStages);
+      if (lane == 0 && !failed) issue(pos + kRingStages, next_head);
     }
     if (__any_sync(0xffffffffu, failed)) {
       // A bounded wait expired.  Lane 0 reports it and lets every copy that

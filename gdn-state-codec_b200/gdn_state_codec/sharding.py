@@ -4,9 +4,10 @@
 GDN recurrent state is independent per request slot, so the codec shards by
 slot with no data-path collective: rank r owns a contiguous block of global
 slot ids and touches only its own HBM.  The only cross-rank operations are
-host-side plumbing: a barrier around timed regions and the max over ranks of
-a device-measured time.  They work with any torch.distributed backend (NCCL
-on the GPU box, gloo in CPU tests).
+host-side plumbing: a barrier around timed regions, the max over ranks of a
+device-measured time and the gathering of per-rank figures for the report.
+They run on a host (gloo) process group, on the GPU box as in the CPU tests,
+so no NCCL communicator is created at all.
 """
 
 from __future__ import annotations
@@ -82,3 +83,25 @@ def max_over_ranks(value: float, device=None) -> float:
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def sum_over_ranks(value: float, device=None) -> float:
+    """Sum of a per-rank count (e.g. parity mismatches found by each rank)."""
+    dist = _distributed()
+    if dist is None or dist.get_world_size() == 1:
+        return float(value)
+    import torch
+
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def gather_over_ranks(value) -> list:
+    """Every rank's value, in rank order (a list of one for a single process)."""
+    dist = _distributed()
+    if dist is None or dist.get_world_size() == 1:
+        return [value]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, value)
+    return out

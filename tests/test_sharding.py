@@ -78,8 +78,9 @@ def _rank_main(rank: int, world: int, port: int, total_slots: int, queue) -> Non
         z, c, b = encode_slots(shard.base, shard.count)
         sharding.barrier()
         slowest = sharding.max_over_ranks(0.5 + rank)
-        gathered = [None] * world
-        dist.all_gather_object(gathered, (shard.base, shard.count, z, c, b))
+        assert sharding.sum_over_ranks(1 + rank) == world * (world + 1) / 2
+        assert sharding.gather_over_ranks({"rank": rank}) == [{"rank": r} for r in range(world)]
+        gathered = sharding.gather_over_ranks((shard.base, shard.count, z, c, b))
         assert sharding.world_size() == world
         dist.destroy_process_group()
         queue.put((rank, "ok", slowest, gathered if rank == 0 else None))
