@@ -832,9 +832,60 @@ def decode_token_latency(codec, torch, device, stream, tokens: int = 15):
     end.synchronize()
     graph_us = start.elapsed_time(end) / tokens * 1e3
     del graph
+    runtime = plugin_runtime_token(torch, device, stream, tokens)
     return {"layers": LAYERS, "heads_per_layer": HEADS, "tokens": tokens,
             "eager_us_per_token": eager_us, "graph_us_per_token": graph_us,
-            "launches_per_token": LAYERS}
+            "launches_per_token": LAYERS, "plugin_runtime": runtime}
+
+
+def plugin_runtime_token(torch, device, stream, tokens: int = 15):
+    """The plugin runtime's own decode path (gdn_state_codec.runtime, the
+    reference's runtime.py:750-845 on CUDA): one GdnStateCodecRuntime per
+    layer, one request slot, `step` called per layer per token, eagerly.
+    Reports device time per token (CUDA events) and host time per token and
+    per step call (wall clock around the 30 calls, after warm-up)."""
+    from gdn_state_codec import _native
+    from gdn_state_codec import runtime as runtime_mod
+    from gdn_state_codec.config import GdnStateCodecExperiment
+
+    experiment = GdnStateCodecExperiment(_native.library_dir(), "replace", "quant_only", 0,
+                                         "vector")
+    gen = torch.Generator(device=device).manual_seed(23)
+    layers = []
+    for layer in range(LAYERS):
+        rt = runtime_mod.GdnStateCodecRuntime(experiment, f"model.layers.{layer}.linear_attn")
+        ssm = torch.randn((2, HEADS, 128, 128), generator=gen, device=device)
+        kq = torch.randn((2, HEADS // 2, 128), generator=gen, device=device)
+        kq = (kq / kq.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        inputs = dict(query=kq[0].reshape(1, 1, HEADS // 2, 128).contiguous(),
+                      key=kq[1].reshape(1, 1, HEADS // 2, 128).contiguous(),
+                      value=torch.randn((1, 1, HEADS, 128), generator=gen,
+                                        device=device).to(torch.bfloat16),
+                      log_decay=-0.05 * torch.rand((1, 1, HEADS), generator=gen, device=device),
+                      beta=torch.rand((1, 1, HEADS), generator=gen,
+                                      device=device).to(torch.bfloat16))
+        layers.append((rt, ssm, inputs))
+
+    def token():
+        for rt, ssm, inputs in layers:
+            rt.step(ssm, 1, query_scale=128 ** -0.5, **inputs)
+
+    token()  # slot encode and first step
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host = []
+    start.record(stream)
+    for _ in range(tokens):  # 15 more steps: the window never needs a refit
+        t0 = time.perf_counter()
+        token()
+        host.append(time.perf_counter() - t0)
+    end.record(stream)
+    end.synchronize()
+    device_us = start.elapsed_time(end) / tokens * 1e3
+    host_us = statistics.median(host) * 1e6
+    return {"device_us_per_token": device_us, "host_us_per_token": host_us,
+            "host_us_per_step_call": host_us / LAYERS,
+            "path": "gdn_state_codec.runtime.GdnStateCodecRuntime.step per layer, eager"}
 
 
 def decode_measure(codec, torch, device, barrier, max_over_ranks, slots, windows: int = 4,
