@@ -31,14 +31,22 @@ def test_profiles_folder_holds_text_summaries_only():
 @pytest.mark.parametrize("summary", SUMMARIES, ids=lambda p: p.name)
 def test_summary_command_runs_committed_files(summary):
     command = _command(summary.read_text())
-    for part in re.split(r"&&|>", command):
+    for part in re.split(r"&&|>|;", command):
         words = shlex.split(part)
         if not words:
             continue
-        if words[0] == "ncu":
+        if words[0] == "timeout":  # a bound around the command: timeout [-k N] SECONDS ...
+            words = words[words.index("python"):] if "python" in words else []
+        if words[0:1] == ["ncu"]:
             assert "--clock-control" in words and \
                 words[words.index("--clock-control") + 1] == "none", part
             words = words[words.index("python"):] if "python" in words else []
+        if words[:3] == ["python", "-m", "pytest"]:
+            for path in (w for w in words[3:] if not w.startswith("-")):
+                assert (ROOT / path).exists(), path
+            continue
+        if words[:3] == ["python", "-m", "torch.distributed.run"]:
+            words = ["python"] + words[words.index("bench.py"):]
         if words[:1] == ["python"]:
             assert words[1] == "bench.py", part
             assert (ROOT / words[1]).is_file()
