@@ -803,4 +803,28 @@ int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
              : gdnsc::kLaunchFailed;
 }
 
+// Test support: the dense fp32 step with its first bounded wait made to run
+// out (barrier armed, no copy issued).
+int32_t statecentric_gdn_state_codec_fp32_gdn_step_wait_selftest_v1(
+    void* stream, float* dense_state, const float* decay, const uint16_t* key,
+    const uint16_t* read, const uint16_t* query, const uint16_t* value, float* output,
+    uint32_t states, uint64_t limit_ns) {
+  if (dense_state == nullptr || decay == nullptr || key == nullptr || read == nullptr ||
+      query == nullptr || value == nullptr || output == nullptr || states == 0u ||
+      limit_ns == 0u || limit_ns > gdnsc::kWaitLimitNs || !gdnsc::aligned16(dense_state) ||
+      !gdnsc::aligned4(decay) || !gdnsc::aligned2(key) || !gdnsc::aligned2(read) ||
+      !gdnsc::aligned2(query) || !gdnsc::aligned2(value) || !gdnsc::aligned4(output)) {
+    return gdnsc::kBadArgs;
+  }
+  const gdnsc::DeviceSetup* s = gdnsc::device_setup();
+  if (s == nullptr) return gdnsc::kSetupFailed;
+  gdnsc::DenseStepParams p{dense_state, decay, key, read, query, value, output, states};
+  p.wait_limit_ns = limit_ns;
+  p.arm_only = 1u;
+  return gdnsc::launch_dense_step(p, gdnsc::grid_for(states, s->sms, s->window.dense),
+                                  static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? gdnsc::kOk
+             : gdnsc::kLaunchFailed;
+}
+
 }  // extern "C"

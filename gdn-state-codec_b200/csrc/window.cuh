@@ -616,6 +616,11 @@ struct DenseStepParams {
   const uint16_t* values;
   float* outputs;            // [heads][128]
   uint64_t heads;
+  uint64_t wait_limit_ns = kWaitLimitNs;  // limit of every bounded wait
+  // Test support (fp32_gdn_step_wait_selftest_v1): the first head's barrier
+  // is armed for bytes that are never copied, so the first wait runs out with
+  // nothing in flight and the block returns before it writes anything.
+  uint32_t arm_only = 0u;
 };
 
 constexpr int kDenseStepBlocksPerSm = 3;
@@ -644,7 +649,11 @@ __global__ void __launch_bounds__(kWinThreads, kDenseStepBlocksPerSm)
   if (t == 0) {
     mbar_init(&sh.full, 1);
     fence_mbar_init();
-    dense_step_issue(p, sh, blockIdx.x);  // the grid never exceeds the head count
+    if (p.arm_only != 0u) {
+      mbar_expect_tx(&sh.full, kElements * sizeof(float));  // test support: nothing lands
+    } else {
+      dense_step_issue(p, sh, blockIdx.x);  // the grid never exceeds the head count
+    }
   }
   __syncthreads();
   uint32_t parity = 0;
@@ -657,13 +666,13 @@ __global__ void __launch_bounds__(kWinThreads, kDenseStepBlocksPerSm)
     const float decay = __ldg(p.decay + head);
     const uint32_t phase = parity;
     parity ^= 1u;
-    const bool landed = mbar_wait_bounded(&sh.full, phase);
+    const bool landed = mbar_wait_bounded(&sh.full, phase, p.wait_limit_ns);
     if (__syncthreads_or(!landed)) {  // token vectors published; uniform result
       // A bounded wait expired: report it, let the copy land (again bounded)
       // so that it no longer targets this block, and stop.
       if (t == 0) {
         report(nullptr, kStatusWaitTimeout);
-        (void)mbar_wait_bounded(&sh.full, phase);
+        (void)mbar_wait_bounded(&sh.full, phase, p.wait_limit_ns);
       }
       return;
     }

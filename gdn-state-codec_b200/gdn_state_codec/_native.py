@@ -63,6 +63,7 @@ SIGNATURES: dict[str, list] = {
         [_vp, _vp, _u64, _u32, _u32, _u32, _u32],
     "statecentric_gdn_state_codec_division_selftest_v1": [_vp, _vp, _vp, _vp, _u64],
     "statecentric_gdn_state_codec_quantize_wait_selftest_v1": [_vp] * 5 + [_u32, _u64, _vp],
+    "statecentric_gdn_state_codec_fp32_gdn_step_wait_selftest_v1": [_vp] * 8 + [_u32, _u64],
     "statecentric_gdn_state_codec_encoded_projection_wait_selftest_v1":
         [_vp] * 6 + [_u32, _u64, _vp],
     # windowed decode (gdn_state_codec_windowed_gdn_kernel.h)

@@ -99,6 +99,18 @@ int32_t statecentric_gdn_state_codec_fp32_gdn_step_launch_v1(
     const uint16_t* read, const uint16_t* query, const uint16_t* value,
     float* output, uint32_t states);
 
+/* Test support for the failure path (no counterpart in the reference, which
+ * has no bounded device waits): fp32_gdn_step_launch_v1 launched with every
+ * block's first landing barrier armed for a copy that is never issued.  Each
+ * block's bounded wait runs out after `limit_ns` nanoseconds (0 < limit_ns <=
+ * 2e9), bit 1 (value 2) of the sticky error word is set, and the blocks return
+ * before writing any state or output.  No copy is in flight, so the CUDA
+ * context stays usable. */
+int32_t statecentric_gdn_state_codec_fp32_gdn_step_wait_selftest_v1(
+    void* stream, float* dense_state, const float* decay, const uint16_t* key,
+    const uint16_t* read, const uint16_t* query, const uint16_t* value,
+    float* output, uint32_t states, uint64_t limit_ns);
+
 /* Boundary refit (reference header :48-60): folds each head's window (its
  * `position` records, normally 16) into a new INT8 boundary plus binary16
  * compensators in the next_* buffers, then clears the records (decay, keys

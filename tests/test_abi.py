@@ -192,6 +192,11 @@ def test_wait_selftest_entry_points_validate():
     assert call(p, n, a, a, a, a, a, 1, 0, a) == BAD_ARGS
     assert call(p, n, a, a, a, n, a, 1, 1000, a) == BAD_ARGS        # no queries
     assert call(p, n, a, a, a, a, a, 0, 1000, a) == BAD_ARGS
+    d = "fp32_gdn_step_wait_selftest_v1"
+    assert call(d, n, a, a, a, a, a, a, a, 1, 0) == BAD_ARGS            # zero limit
+    assert call(d, n, a, a, a, a, a, a, a, 1, 2_000_000_001) == BAD_ARGS
+    assert call(d, n, a, a, a, a, a, a, a, 0, 1000) == BAD_ARGS         # no states
+    assert call(d, n, m, a, a, a, a, a, a, 1, 1000) == BAD_ARGS         # misaligned state
 
 
 def _window(a=ALIGNED):

@@ -1,11 +1,12 @@
 """The bounded-wait failure path on the GPU, made to happen without a fault.
 
-The quantizer and the capsule-code projection stream their inputs through
-shared memory with bulk copies completing on mbarriers, and every wait on
-those barriers gives up after a limit (2 s in production), reports bit 1 of
-the caller's status word and of the sticky device word, and lets the kernel
-return.  The test-support launchers (`quantize_wait_selftest_v1`,
-`encoded_projection_wait_selftest_v1`) run the same kernels with the barriers
+The quantizer, the capsule-code projection and the dense fp32 step stream
+their inputs through shared memory with bulk copies completing on mbarriers,
+and every wait on those barriers gives up after a limit (2 s in production),
+reports bit 1 of the caller's status word and of the sticky device word, and
+lets the kernel return.  The test-support launchers
+(`quantize_wait_selftest_v1`, `encoded_projection_wait_selftest_v1`,
+`fp32_gdn_step_wait_selftest_v1`) run the same kernels with the barriers
 armed for a copy that is never issued, so each wait runs out (a flag that
 nothing sets) after a 1 ms limit with nothing in flight.  The test checks the
 status bits, that the context still works, and that the next ordinary launch
@@ -88,4 +89,41 @@ def test_projection_wait_runs_out_and_reports(heads):
     z, c, b = check_quantize_exact(states, enc)
     want = oracle.project(z, c, b, queries.float().cpu().numpy().reshape(-1, 128))
     assert np.array_equal(out.cpu().numpy().reshape(-1, 128), want)
+    assert codec.device_error(DEV) & TIMEOUT_BIT == 0
+
+
+@pytest.mark.parametrize("heads", [4, 600])
+def test_dense_step_wait_runs_out_and_reports(heads):
+    """The dense fp32 step (fp32_gdn_step_launch_v1) on the same failure
+    path: the wait on its first landing buffer runs out, bit 1 of the sticky
+    word is set, and no state or output is written."""
+    codec.device_error(DEV, clear=True)
+    states = codec.synthesize_states(1, 1, heads, device=DEV, seed=13).reshape(heads, 128, 128)
+    before = states.clone()
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    decay = 0.9 + 0.1 * torch.rand(heads, generator=gen, device=DEV)
+
+    def vectors():
+        return (torch.randn((heads, 128), generator=gen, device=DEV) / 11.3).half()
+
+    keys, reads, queries, values = vectors(), vectors(), vectors(), vectors()
+    out = torch.full((heads, 128), 7.0, device=DEV)
+    rc = _native.call("statecentric_gdn_state_codec_fp32_gdn_step_wait_selftest_v1", stream(),
+                      ptr(states), ptr(decay), ptr(keys), ptr(reads), ptr(queries), ptr(values),
+                      ptr(out), heads, LIMIT_NS)
+    assert rc == 0
+    torch.cuda.synchronize(DEV)
+    assert codec.device_error(DEV, clear=True) & TIMEOUT_BIT
+    assert torch.equal(states.view(torch.int32), before.view(torch.int32))
+    assert bool((out == 7.0).all())
+    # The next ordinary step is exact against the oracle and reports nothing.
+    got = codec.dense_step(states, decay, keys, reads, queries, values)
+    torch.cuda.synchronize(DEV)
+    host = before.cpu().numpy().copy()
+    f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+    d, k, r, q, v = decay.cpu().numpy(), f32(keys), f32(reads), f32(queries), f32(values)
+    want = np.stack([oracle.dense_step(host[i], d[i], k[i], r[i], q[i], v[i])
+                     for i in range(heads)])
+    assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(states.cpu().numpy().view(np.uint32), host.view(np.uint32))
     assert codec.device_error(DEV) & TIMEOUT_BIT == 0
