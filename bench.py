@@ -1191,8 +1191,8 @@ def e2e_measure(codec, torch, states, layout, slots, heads, args, device, barrie
             "copy_rates_per_rank": per_rank,
             "limiter": (f"host copies: a step moves {nbytes / 1e9:.2f} GB each way per rank; "
                         f"with every rank copying both ways at once the slowest rank moves "
-                        f"{slowest:.1f} GB/s each way, {copy_ms:.1f} ms of the {ms:.1f} ms step "
-                        f"(the device kernels take about 2 ms)")}
+                        f"{slowest:.1f} GB/s each way, so the copies alone take {copy_ms:.1f} ms; "
+                        f"the step, with its device kernels overlapped, takes {ms:.1f} ms")}
 
 
 if __name__ == "__main__":
