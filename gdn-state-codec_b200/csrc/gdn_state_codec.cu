@@ -85,10 +85,10 @@ const DeviceSetup* device_setup() {
   }
   if (prepare_fit(&s.fit_blocks) != cudaSuccess || s.fit_blocks < 1) return nullptr;
   if (prepare_capsule() != cudaSuccess) return nullptr;
-  if (prepare_window(&s.window) != cudaSuccess || s.window.fold < 1 ||
-      s.window.dense < 1 || s.window.window_dense < 1 || s.window.step[0][0] < 1 ||
-      s.window.step[0][1] < 1 ||
-      s.window.step[1][0] < 1 || s.window.step[1][1] < 1) {
+  if (prepare_window(&s.window) != cudaSuccess || s.window.fold < 1 || s.window.dense < 1 ||
+      s.window.window_dense[0] < 1 || s.window.window_dense[1] < 1 ||
+      s.window.step[0][0] < 1 || s.window.step[0][1] < 1 || s.window.step[1][0] < 1 ||
+      s.window.step[1][1] < 1) {
     return nullptr;
   }
   s.ready = true;
@@ -774,8 +774,8 @@ int32_t statecentric_gdn_state_codec_window_boundary_launch_v1(
   // iterations the fit kernel folds and fits each head in shared memory.
   const cudaError_t err =
       power_iterations == 0u
-          ? gdnsc::launch_window_dense(fp, gdnsc::grid_for(states, s->sms, s->window.window_dense),
-                                       st)
+          ? gdnsc::launch_window_dense(
+                fp, gdnsc::grid_for(states, s->sms, s->window.window_dense[w.ck != nullptr]), st)
           : gdnsc::launch_window_fold(fp, gdnsc::grid_for(states, s->sms, s->window.fold), st);
   if (err != cudaSuccess) return gdnsc::kLaunchFailed;
   return gdnsc::run_quantize(stream, true, gdnsc::kFused, residual_workspace, nullptr,

@@ -423,27 +423,32 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
 }
 
 // Quant-only refit (no power iterations): the window's DenseState streamed
-// straight to the workspace, one 256-thread CTA per head.  Thread t owns the
-// key pair (2 (t mod 64), 2 (t mod 64) + 1) of rows v = t / 64 + 4 i, so an
-// element pair is adjacent in the provider layout [v][k]: its two codes are
-// one 16-bit word, its smoothing, record keys and compensator keys are natural
-// register pairs, and it is written with one 8-byte store.  The per-row
-// factors (scale, compensator values, record corrections) are the same for
-// both elements and for the whole warp (a warp holds one row), so shared
-// memory keeps them duplicated, (x, x), and one broadcast load yields the
-// packed operand.  Every element follows the reference order (dequantize,
-// compensators by rank, records oldest first) in packed fp32x2 arithmetic,
-// each product rounded before its add.
+// straight to the workspace, one 256-thread CTA per head in two passes of 64
+// rows.  Lane l = t mod 16 owns keys 4l..4l+3 and 64+4l..64+4l+3, and thread
+// t owns rows 4 (t / 16) + i (i < 4) of each pass: 32 elements, held in
+// registers as 16 adjacent key pairs of the provider layout [v][k] while the
+// whole window is applied.  Records are the outer loop, so each record's
+// decay, key quads and row corrections are one broadcast load per use and
+// serve 16 element pairs; the per-record work is then the reference's two
+// rounded products and one add per element, in packed fp32x2 arithmetic.
+// Every element follows the reference order (dequantize, compensators by
+// rank, records oldest first); the 16-lane row segments keep both the
+// shared-memory key loads and the 16-byte workspace stores contiguous.
 constexpr int kDenseThreads = 256;
-constexpr int kDensePairs = kKeys / 2;                    // threads per row
-constexpr int kDenseRowGroups = kDenseThreads / kDensePairs;  // rows in flight per CTA
+constexpr int kDenseLanes = 16;                                             // threads across a row
+constexpr int kDenseRows = 4;                                               // rows per thread per pass
+constexpr int kDenseRowsPerPass = kDenseThreads / kDenseLanes * kDenseRows;  // 64
+constexpr int kDensePasses = kValues / kDenseRowsPerPass;                   // 2
+static_assert(kDenseLanes * 8 == kKeys && kDensePasses * kDenseRowsPerPass == kValues,
+              "dense refit tile");
+static_assert(kWindow * kDenseLanes == kDenseThreads, "one thread per record chunk of 8");
 
 struct __align__(16) WindowDenseShared {
-  int8_t codes[kElements];              // the head's codes, provider [v][k]
-  float4 rc[kWindow / 2][kValues];      // (rc_u, rc_u, rc_u+1, rc_u+1) per row, u even
-  float4 cv[2][kValues];                // (V0, V0, V1, V1), (V2, V2, V3, V3) per row
-  f2 b[kValues];                        // (b, b) per row
-  float4 dd[kWindow / 2];               // (d_u, d_u, d_u+1, d_u+1), u even
+  float rk[kWindow][kKeys];      // record keys (fp32), u < position only
+  f2 rc[kWindow][kValues];       // (rc, rc) per record and row, u < position only
+  f2 d[kWindow];                 // (decay, decay), u < position only
+  float ck[kRank][kKeys];        // compensator keys, rank-major (compensated boundary)
+  f2 cv[kRank][kValues];         // (V, V) per rank and row
 };
 
 // a / 127 for both lanes, exact for every float (the two-term reciprocal
@@ -458,134 +463,196 @@ __device__ __forceinline__ f2 div127x2_any(f2 a) {
 __device__ __forceinline__ f2 lo_pair(float4 v) { return pack2(v.x, v.y); }
 __device__ __forceinline__ f2 hi_pair(float4 v) { return pack2(v.z, v.w); }
 
-// The workspace rows of one thread (rows row0 + 4 i, keys 2 kp, 2 kp + 1).
-// Returns an accumulator that stays +0 while every element is finite and
-// becomes NaN otherwise (x * 0 is NaN exactly for infinite or NaN x).
+// The dequantized boundary of one row segment of four keys, before any
+// compensator: codes word `zw`, smoothing pairs (c0, c1), (c2, c3) in `c`,
+// scale pair `bb`.  With compensators to follow, the product is rounded
+// before their adds: a single-use mul.f32x2 feeding an add.f32x2 would be
+// contracted into one fma.  The +0 addend can turn a -0 product into +0,
+// which the INT8 stage encodes identically.
 template <bool kComp>
-__device__ __forceinline__ f2 dense_rows(const WindowDenseShared& sh, f2 cc, bool c_safe,
-                                         const f2 (&rk)[kWindow], const f2 (&ck)[kRank],
-                                         int row0, int kp, float* workspace) {
-  const uint16_t* codes = reinterpret_cast<const uint16_t*>(sh.codes) + kp;  // [v][pair]
-  f2* out = reinterpret_cast<f2*>(workspace) + kp;
-  const f2 magic = pack2(kCodeMagic, kCodeMagic);
-  const f2 zero = pack2(0.0F, 0.0F);
-  f2 flags = zero;
-#pragma unroll 2
-  for (int i = 0; i < kValues / kDenseRowGroups; ++i) {
-    const int v = row0 + kDenseRowGroups * i;
-    const uint32_t biased = static_cast<uint32_t>(codes[v * kDensePairs]) ^ kCodeBias;
-    const f2 z = sub2(pack2(code_magic(biased, 0), code_magic(biased, 1)), magic);
-    const f2 cz = mul2(cc, z);
-    f2 q = div127x2(cz);
-    if (!c_safe) q = div127x2_any(cz);  // a smoothing below 2^-112 in magnitude
-    // Rounded before the compensator adds: a single-use mul.f32x2 feeding an
-    // add.f32x2 would be contracted into one fma.  The +0 addend can turn a
-    // -0 product into +0, which the INT8 stage encodes identically.
-    f2 val = mul2_for_add(q, sh.b[v]);
-    if constexpr (kComp) {
-      const float4 c01 = sh.cv[0][v], c23 = sh.cv[1][v];
-      val = add2(val, mul2_for_add(ck[0], lo_pair(c01)));
-      val = add2(val, mul2_for_add(ck[1], hi_pair(c01)));
-      val = add2(val, mul2_for_add(ck[2], lo_pair(c23)));
-      val = add2(val, mul2_for_add(ck[3], hi_pair(c23)));
-    }
-#pragma unroll
-    for (int j = 0; j < kWindow / 2; ++j) {
-      const float4 d = sh.dd[j], r = sh.rc[j][v];
-      val = add2(mul2_for_add(lo_pair(d), val), mul2_for_add(rk[2 * j], lo_pair(r)));
-      val = add2(mul2_for_add(hi_pair(d), val), mul2_for_add(rk[2 * j + 1], hi_pair(r)));
-    }
-    flags = fma2(val, zero, flags);
-    __stcg(reinterpret_cast<unsigned long long*>(out + v * kDensePairs), val);
+__device__ __forceinline__ void dense_boundary(uint32_t zw, float4 c, bool c_safe, f2 bb,
+                                               f2& s01, f2& s23) {
+  f2 z01, z23;
+  unpack_codes(zw, z01, z23);
+  const f2 cz01 = mul2(lo_pair(c), z01), cz23 = mul2(hi_pair(c), z23);
+  f2 q01 = div127x2(cz01), q23 = div127x2(cz23);
+  if (!c_safe) {  // a smoothing below 2^-112 in magnitude
+    q01 = div127x2_any(cz01);
+    q23 = div127x2_any(cz23);
   }
-  return flags;
+  if constexpr (kComp) {
+    s01 = mul2_for_add(q01, bb);
+    s23 = mul2_for_add(q23, bb);
+  } else {
+    s01 = mul2(q01, bb);
+    s23 = mul2(q23, bb);
+  }
 }
 
+// Four CTAs per SM (64 registers) for the quant-only boundary; the
+// compensated one keeps three so that its rank loop does not spill.
 template <bool kComp>
-__global__ void __launch_bounds__(kDenseThreads, 3) window_dense_kernel(FoldParams p) {
+__global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
+    window_dense_kernel(FoldParams p) {
   __shared__ WindowDenseShared sh;
   const int t = threadIdx.x;
-  const int kp = t % kDensePairs;          // keys 2 kp, 2 kp + 1
-  const int row0 = t / kDensePairs;        // rows row0 + 4 i
+  const int lane = t % kDenseLanes;
+  const int ka = 4 * lane, kb = kKeys / 2 + 4 * lane;
+  const int row0 = kDenseRows * (t / kDenseLanes);
+  const f2 zero = pack2(0.0F, 0.0F);
   for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
     const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
     const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
     const uint64_t rbase = head * kWindow;
-    // ---- gather: codes, records, scales, compensators ------------------------
+    const int8_t* codes = p.w.codes + head * kElements;
+    // ---- records (u < position) to shared memory: 8 keys and 8 rows a thread --
     {
-      const uint4* src = reinterpret_cast<const uint4*>(p.w.codes + head * kElements);
+      const int u = t / kDenseLanes, k8 = 8 * (t % kDenseLanes);
+      if (u < np) {
+        const uint4 kw = __ldcg(reinterpret_cast<const uint4*>(p.w.record_keys +
+                                                               (rbase + u) * kKeys + k8));
+        const uint4 cw = __ldcg(reinterpret_cast<const uint4*>(p.w.record_corrections +
+                                                               (rbase + u) * kValues + k8));
+        const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
+        const uint32_t cws[4] = {cw.x, cw.y, cw.z, cw.w};
+        float4* rk = reinterpret_cast<float4*>(&sh.rk[u][k8]);
+        float4* rc = reinterpret_cast<float4*>(&sh.rc[u][k8]);
 #pragma unroll
-      for (int i = 0; i < kElements / 16 / kDenseThreads; ++i) {
-        reinterpret_cast<uint4*>(sh.codes)[t + kDenseThreads * i] = __ldcs(src + t + kDenseThreads * i);
+        for (int j = 0; j < 2; ++j) {
+          rk[j] = make_float4(half_to_float(kws[2 * j] & 0xFFFFu), half_to_float(kws[2 * j] >> 16),
+                              half_to_float(kws[2 * j + 1] & 0xFFFFu),
+                              half_to_float(kws[2 * j + 1] >> 16));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = half_to_float(cws[j] & 0xFFFFu), hi = half_to_float(cws[j] >> 16);
+          rc[j] = make_float4(lo, lo, hi, hi);
+        }
+      }
+      if (t < np) {
+        const float d = __ldcg(p.w.record_decay + rbase + t);
+        sh.d[t] = pack2(d, d);
       }
     }
-    // Records past the position are identity records (decay 1, zero key and
-    // correction): v -> RN(1 v) + RN(0 0) = v, except that a -0 may become +0,
-    // which the INT8 stage maps to the same codes, smoothing and scales.  The
-    // record loop below is then free of position tests.
-    for (int i = t; i < (kWindow / 2) * kValues; i += kDenseThreads) {
-      const int u = 2 * (i / kValues), v = i % kValues;
-      const uint16_t* rcs = p.w.record_corrections + rbase * kValues + v;
-      const float a = u < np ? half_to_float(__ldcg(rcs + u * kValues)) : 0.0F;
-      const float c = u + 1 < np ? half_to_float(__ldcg(rcs + (u + 1) * kValues)) : 0.0F;
-      sh.rc[u / 2][v] = make_float4(a, a, c, c);
-    }
-    if (t < kValues) {
-      const float b = __ldg(p.w.scales + head * kValues + t);
-      sh.b[t] = pack2(b, b);
-      if constexpr (kComp) {
-        const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + t) * kRank));
-        const float v0 = half_to_float(vw.x & 0xFFFFu), v1 = half_to_float(vw.x >> 16);
-        const float v2 = half_to_float(vw.y & 0xFFFFu), v3 = half_to_float(vw.y >> 16);
-        sh.cv[0][t] = make_float4(v0, v0, v1, v1);
-        sh.cv[1][t] = make_float4(v2, v2, v3, v3);
-      }
-    }
-    if (t < kWindow / 2) {
-      const float d0 = 2 * t < np ? __ldcg(p.w.record_decay + rbase + 2 * t) : 1.0F;
-      const float d1 = 2 * t + 1 < np ? __ldcg(p.w.record_decay + rbase + 2 * t + 1) : 1.0F;
-      sh.dd[t] = make_float4(d0, d0, d1, d1);
-    }
-    f2 rk[kWindow];  // (key 2 kp, key 2 kp + 1) of every record
-#pragma unroll
-    for (int u = 0; u < kWindow; ++u) {
-      uint32_t w = 0u;
-      if (u < np) w = __ldcg(reinterpret_cast<const uint32_t*>(p.w.record_keys + (rbase + u) * kKeys) + kp);
-      rk[u] = pack2(half_to_float(w & 0xFFFFu), half_to_float(w >> 16));
-    }
-    f2 ck[kRank] = {0ull, 0ull, 0ull, 0ull};
     if constexpr (kComp) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.w.ck + head * kKeys * kRank) + kp);
-      // keys 2 kp (ranks 0..3 in w.x, w.y) and 2 kp + 1 (w.z, w.w)
-      ck[0] = pack2(half_to_float(w.x & 0xFFFFu), half_to_float(w.z & 0xFFFFu));
-      ck[1] = pack2(half_to_float(w.x >> 16), half_to_float(w.z >> 16));
-      ck[2] = pack2(half_to_float(w.y & 0xFFFFu), half_to_float(w.w & 0xFFFFu));
-      ck[3] = pack2(half_to_float(w.y >> 16), half_to_float(w.w >> 16));
+      if (t < kKeys) {
+        const uint2 kw = __ldg(reinterpret_cast<const uint2*>(p.w.ck + (head * kKeys + t) * kRank));
+        sh.ck[0][t] = half_to_float(kw.x & 0xFFFFu);
+        sh.ck[1][t] = half_to_float(kw.x >> 16);
+        sh.ck[2][t] = half_to_float(kw.y & 0xFFFFu);
+        sh.ck[3][t] = half_to_float(kw.y >> 16);
+      } else {
+        const int v = t - kKeys;
+        const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.w.cv + (head * kValues + v) * kRank));
+        const float vm[kRank] = {half_to_float(vw.x & 0xFFFFu), half_to_float(vw.x >> 16),
+                                 half_to_float(vw.y & 0xFFFFu), half_to_float(vw.y >> 16)};
+#pragma unroll
+        for (int m = 0; m < kRank; ++m) sh.cv[m][v] = pack2(vm[m], vm[m]);
+      }
     }
-    const f2 cc = *reinterpret_cast<const f2*>(p.w.smoothing + head * kKeys + 2 * kp);
     __syncthreads();
-    // ---- the window is about to be folded: clear it --------------------------
-    for (int i = t; i < kWindow * kKeys; i += kDenseThreads) {
-      p.w.record_keys[rbase * kKeys + i] = 0;
-      p.w.record_corrections[rbase * kValues + i] = 0;
+    // ---- the window is about to be folded: clear it ------------------------
+    {
+      const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(p.w.record_keys + rbase * kKeys)[t] = z4;
+      reinterpret_cast<uint4*>(p.w.record_corrections + rbase * kValues)[t] = z4;
+      if (t < kWindow) p.w.record_decay[rbase + t] = 0.0F;
+      if (t == 0) p.w.positions[head * kPositionStride] = 0u;
+      if (t < kKeys) {
+        reinterpret_cast<uint2*>(p.next_ck + (head * kKeys + t) * kRank)[0] = make_uint2(0u, 0u);
+      } else {
+        reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t - kKeys) * kRank)[0] =
+            make_uint2(0u, 0u);
+      }
     }
-    if (t < kWindow) p.w.record_decay[rbase + t] = 0.0F;
-    if (t == 0) p.w.positions[head * kPositionStride] = 0u;
-    if (t < kKeys) {
-      reinterpret_cast<uint2*>(p.next_ck + (head * kKeys + t) * kRank)[0] = make_uint2(0u, 0u);
-      reinterpret_cast<uint2*>(p.next_cv + (head * kValues + t) * kRank)[0] = make_uint2(0u, 0u);
-    }
-    // ---- dense rows ----------------------------------------------------------
-    // With this thread's smoothing pair at least 2^-112 in magnitude, zero or
-    // not finite, every product c z is zero or at least 2^-112 in magnitude
-    // (codes are integers), where the two-term reciprocal division is exact;
+    // With this thread's smoothing at least 2^-112 in magnitude, zero or not
+    // finite, every product c z is zero or at least 2^-112 in magnitude (codes
+    // are integers), where the two-term reciprocal division is exact;
     // otherwise each product is checked.
-    const float c0 = lo2(cc), c1 = hi2(cc);
-    const bool c_safe = (fabsf(c0) >= kDiv127Safe || c0 == 0.0F || c0 != c0) &&
-                        (fabsf(c1) >= kDiv127Safe || c1 == 0.0F || c1 != c1);
+    bool c_safe = true;
+    {
+      const float4 ca = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + ka));
+      const float4 cb = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + kb));
+      const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c_safe = c_safe && (fabsf(cs[j]) >= kDiv127Safe || cs[j] == 0.0F || cs[j] != cs[j]);
+      }
+    }
+    // x * 0 + flags stays +0 while every element is finite and becomes NaN
+    // otherwise (x * 0 is NaN exactly for infinite or NaN x).
+    f2 flags = zero;
     float* rows = p.workspace + head * kElements;
-    const f2 flags = dense_rows<kComp>(sh, cc, c_safe, rk, ck, row0, kp, rows);
+#pragma unroll 1
+    for (int pass = 0; pass < kDensePasses; ++pass) {
+      const int v0 = pass * kDenseRowsPerPass + row0;
+      uint32_t za[kDenseRows], zb[kDenseRows];
+#pragma unroll
+      for (int i = 0; i < kDenseRows; ++i) {
+        za[i] = ld_cs_u32(codes + (v0 + i) * kKeys + ka);
+        zb[i] = ld_cs_u32(codes + (v0 + i) * kKeys + kb);
+      }
+      // Smoothing reloaded per pass (a cache hit) rather than held across it.
+      const float4 ca = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + ka));
+      const float4 cb = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + kb));
+      const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.w.scales + head * kValues + v0));
+      const float bs[kDenseRows] = {b4.x, b4.y, b4.z, b4.w};
+      f2 s[kDenseRows][4];  // row i: keys (ka, ka+1), (ka+2, ka+3), (kb, kb+1), (kb+2, kb+3)
+#pragma unroll
+      for (int i = 0; i < kDenseRows; ++i) {
+        const f2 bb = pack2(bs[i], bs[i]);
+        dense_boundary<kComp>(za[i], ca, c_safe, bb, s[i][0], s[i][1]);
+        dense_boundary<kComp>(zb[i], cb, c_safe, bb, s[i][2], s[i][3]);
+      }
+      if constexpr (kComp) {  // compensators by rank: S += RN(K[k][m] V[v][m])
+#pragma unroll
+        for (int m = 0; m < kRank; ++m) {
+          const float4 k4a = *reinterpret_cast<const float4*>(&sh.ck[m][ka]);
+          const float4 k4b = *reinterpret_cast<const float4*>(&sh.ck[m][kb]);
+          const float4 v01 = *reinterpret_cast<const float4*>(&sh.cv[m][v0]);
+          const float4 v23 = *reinterpret_cast<const float4*>(&sh.cv[m][v0 + 2]);
+          const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
+          const f2 vv[kDenseRows] = {lo_pair(v01), hi_pair(v01), lo_pair(v23), hi_pair(v23)};
+#pragma unroll
+          for (int i = 0; i < kDenseRows; ++i) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = add2(s[i][j], mul2_for_add(kk[j], vv[i]));
+          }
+        }
+      }
+      // Records oldest first: S = RN(RN(d S) + RN(key correction)).  Both
+      // products are single-use operands of the add, so both take the
+      // non-contracted form.
+#pragma unroll 8
+      for (int u = 0; u < np; ++u) {
+        const f2 d = sh.d[u];
+        const float4 k4a = *reinterpret_cast<const float4*>(&sh.rk[u][ka]);
+        const float4 k4b = *reinterpret_cast<const float4*>(&sh.rk[u][kb]);
+        const float4 r01 = *reinterpret_cast<const float4*>(&sh.rc[u][v0]);
+        const float4 r23 = *reinterpret_cast<const float4*>(&sh.rc[u][v0 + 2]);
+        const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
+        const f2 rr[kDenseRows] = {lo_pair(r01), hi_pair(r01), lo_pair(r23), hi_pair(r23)};
+#pragma unroll
+        for (int i = 0; i < kDenseRows; ++i) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            s[i][j] = add2(mul2_for_add(d, s[i][j]), mul2_for_add(kk[j], rr[i]));
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kDenseRows; ++i) {
+        float* row = rows + (v0 + i) * kKeys;
+        __stcg(reinterpret_cast<float4*>(row + ka),
+               make_float4(lo2(s[i][0]), hi2(s[i][0]), lo2(s[i][1]), hi2(s[i][1])));
+        __stcg(reinterpret_cast<float4*>(row + kb),
+               make_float4(lo2(s[i][2]), hi2(s[i][2]), lo2(s[i][3]), hi2(s[i][3])));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) flags = fma2(s[i][j], zero, flags);
+      }
+    }
     const bool finite = lo2(flags) == 0.0F && hi2(flags) == 0.0F;
+    // Also the barrier before the next head's records overwrite shared memory.
     if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusWindowNonFinite);
   }
 }
@@ -717,7 +784,7 @@ __global__ void __launch_bounds__(kWinThreads, kDenseStepBlocksPerSm)
 struct WindowBlocks {
   int step[2][2] = {};  // [qwen][comp] blocks per SM
   int fold = 0;
-  int window_dense = 0;
+  int window_dense[2] = {};  // [compensated]
   int dense = 0;
 };
 
@@ -743,7 +810,10 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->fold, window_fold_kernel, kFitThreads,
                                                       window_fold_smem_bytes());
   if (err != cudaSuccess) return err;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense, window_dense_kernel<true>,
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense[0], window_dense_kernel<false>,
+                                                      kDenseThreads, 0);
+  if (err != cudaSuccess) return err;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense[1], window_dense_kernel<true>,
                                                       kDenseThreads, 0);
   if (err != cudaSuccess) return err;
   err = cudaFuncSetAttribute(dense_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

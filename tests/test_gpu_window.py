@@ -247,6 +247,35 @@ def test_refit_of_a_partial_window_matches_oracle(compensators, iterations):
     assert (nxt.compensator_keys is None) == (not compensators and iterations == 0)
 
 
+def test_non_finite_refit_state_sets_the_status_bit():
+    """A binary16 infinity in one head's record correction: the quant-only
+    refit reports bit 4 (non-finite refit state) and not the fit's bit 2, the
+    window is still cleared, and every other head's new boundary is still
+    bit-identical to the oracle."""
+    case = wc.step_probe_case(states=4, position=7)
+    window = window_from_case(case, "provider", False)
+    heads = wc.window_heads(case, "provider", False)
+    window.record_corrections[2, 3, 17] = float("inf")
+    codec.device_error(DEV, clear=True)
+    nxt = codec.window_refit(window, 0)
+    torch.cuda.synchronize()
+    status = codec.device_error(DEV, clear=True)
+    assert status & codec.STATUS_WINDOW_NON_FINITE
+    assert not status & codec.STATUS_FIT_NON_FINITE
+    for h in heads:
+        assert h.fold(0, round_storage=True) == 0
+        h.ck = h.cv = None
+    keep = [0, 1, 3]
+    sub = codec.WindowStates(
+        codec.EncodedStates(nxt.encoded.codes[keep], nxt.encoded.smoothing[keep],
+                            nxt.encoded.scales[keep], "provider"),
+        None, None, nxt.record_decay[keep], nxt.record_keys[keep],
+        nxt.record_corrections[keep], nxt.positions[keep])
+    _assert_boundary(sub, [heads[i] for i in keep], "refit beside a non-finite head")
+    assert bool((window.positions[:, 0] == 0).all())
+    assert bool((window.record_corrections == 0).all())
+
+
 def test_generic_step_sequence_matches_oracle():
     """16 generic (binary16) tokens from an empty window over a rank-4
     boundary, capsule layout: every output and record bit-identical to the
