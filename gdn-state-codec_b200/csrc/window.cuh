@@ -385,16 +385,18 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
     for (int v = 0; v < kValues; ++v) {
       const float z = static_cast<float>(__ldg(codes + v * kKeys + t));  // provider [v][k]
       float value = __fmul_rn(div127_any(__fmul_rn(c_t, z)), ex.b[v]);
+      // Compensator and record products multiply two binary16 values, exact
+      // in fp32, so RN(x + RN(a b)) is fma(a, b, x).
       if (comp) {
         const float4 cvv = ex.cv[v];
-        value = __fadd_rn(value, __fmul_rn(ck_t.x, cvv.x));
-        value = __fadd_rn(value, __fmul_rn(ck_t.y, cvv.y));
-        value = __fadd_rn(value, __fmul_rn(ck_t.z, cvv.z));
-        value = __fadd_rn(value, __fmul_rn(ck_t.w, cvv.w));
+        value = __fmaf_rn(ck_t.x, cvv.x, value);
+        value = __fmaf_rn(ck_t.y, cvv.y, value);
+        value = __fmaf_rn(ck_t.z, cvv.z, value);
+        value = __fmaf_rn(ck_t.w, cvv.w, value);
       }
 #pragma unroll
       for (int u = 0; u < kWindow; ++u) {
-        if (u < np) value = __fadd_rn(__fmul_rn(rd[u], value), __fmul_rn(rk[u], ex.rc[u][v]));
+        if (u < np) value = __fmaf_rn(rk[u], ex.rc[u][v], __fmul_rn(rd[u], value));
       }
       finite = finite && isfinite(value);
       sh.r[t][v] = value;
@@ -429,11 +431,12 @@ __global__ void __launch_bounds__(kFitThreads) window_fold_kernel(FoldParams p) 
 // registers as 16 adjacent key pairs of the provider layout [v][k] while the
 // whole window is applied.  Records are the outer loop, so each record's
 // decay, key quads and row corrections are one broadcast load per use and
-// serve 16 element pairs; the per-record work is then the reference's two
-// rounded products and one add per element, in packed fp32x2 arithmetic.
-// Every element follows the reference order (dequantize, compensators by
-// rank, records oldest first); the 16-lane row segments keep both the
-// shared-memory key loads and the 16-byte workspace stores contiguous.
+// serve 16 element pairs.  The reference's update RN(RN(d S) + RN(k c)) is
+// one rounded product and one fma per element in packed fp32x2 arithmetic,
+// because k c (two binary16 values) is exact in fp32.  Every element follows
+// the reference order (dequantize, compensators by rank, records oldest
+// first); the 16-lane row segments keep both the shared-memory key loads and
+// the 16-byte workspace stores contiguous.
 constexpr int kDenseThreads = 256;
 constexpr int kDenseLanes = 16;                                             // threads across a row
 constexpr int kDenseRows = 4;                                               // rows per thread per pass
@@ -465,11 +468,8 @@ __device__ __forceinline__ f2 hi_pair(float4 v) { return pack2(v.z, v.w); }
 
 // The dequantized boundary of one row segment of four keys, before any
 // compensator: codes word `zw`, smoothing pairs (c0, c1), (c2, c3) in `c`,
-// scale pair `bb`.  With compensators to follow, the product is rounded
-// before their adds: a single-use mul.f32x2 feeding an add.f32x2 would be
-// contracted into one fma.  The +0 addend can turn a -0 product into +0,
-// which the INT8 stage encodes identically.
-template <bool kComp>
+// scale pair `bb`.  Every later use of the result is an fma addend or
+// multiplicand, which no contraction can merge with this product.
 __device__ __forceinline__ void dense_boundary(uint32_t zw, float4 c, bool c_safe, f2 bb,
                                                f2& s01, f2& s23) {
   f2 z01, z23;
@@ -480,13 +480,8 @@ __device__ __forceinline__ void dense_boundary(uint32_t zw, float4 c, bool c_saf
     q01 = div127x2_any(cz01);
     q23 = div127x2_any(cz23);
   }
-  if constexpr (kComp) {
-    s01 = mul2_for_add(q01, bb);
-    s23 = mul2_for_add(q23, bb);
-  } else {
-    s01 = mul2(q01, bb);
-    s23 = mul2(q23, bb);
-  }
+  s01 = mul2(q01, bb);
+  s23 = mul2(q23, bb);
 }
 
 // Four CTAs per SM (64 registers) for the quant-only boundary; the
@@ -601,10 +596,10 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
 #pragma unroll
       for (int i = 0; i < kDenseRows; ++i) {
         const f2 bb = pack2(bs[i], bs[i]);
-        dense_boundary<kComp>(za[i], ca, c_safe, bb, s[i][0], s[i][1]);
-        dense_boundary<kComp>(zb[i], cb, c_safe, bb, s[i][2], s[i][3]);
+        dense_boundary(za[i], ca, c_safe, bb, s[i][0], s[i][1]);
+        dense_boundary(zb[i], cb, c_safe, bb, s[i][2], s[i][3]);
       }
-      if constexpr (kComp) {  // compensators by rank: S += RN(K[k][m] V[v][m])
+      if constexpr (kComp) {  // compensators by rank: S = RN(S + RN(K[k][m] V[v][m]))
 #pragma unroll
         for (int m = 0; m < kRank; ++m) {
           const float4 k4a = *reinterpret_cast<const float4*>(&sh.ck[m][ka]);
@@ -613,16 +608,22 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
           const float4 v23 = *reinterpret_cast<const float4*>(&sh.cv[m][v0 + 2]);
           const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
           const f2 vv[kDenseRows] = {lo_pair(v01), hi_pair(v01), lo_pair(v23), hi_pair(v23)};
+          // K and V are binary16 too: the product is exact, so the add is
+          // one fma.
 #pragma unroll
           for (int i = 0; i < kDenseRows; ++i) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) s[i][j] = add2(s[i][j], mul2_for_add(kk[j], vv[i]));
+            for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], vv[i], s[i][j]);
           }
         }
       }
-      // Records oldest first: S = RN(RN(d S) + RN(key correction)).  Both
-      // products are single-use operands of the add, so both take the
-      // non-contracted form.
+      // Records oldest first: S = RN(RN(d S) + RN(key correction)).  Key and
+      // correction are binary16 values (11-bit significands, magnitudes in
+      // [2^-24, 65504]), so their product has at most 22 significant bits and
+      // lies in fp32's normal range: RN(key correction) = key correction,
+      // and the update is exactly fma(key, correction, RN(d S)) -- two
+      // operations per element instead of three, for every input including
+      // zeros of either sign, infinities and NaN.
 #pragma unroll 8
       for (int u = 0; u < np; ++u) {
         const f2 d = sh.d[u];
@@ -635,9 +636,7 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
 #pragma unroll
         for (int i = 0; i < kDenseRows; ++i) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            s[i][j] = add2(mul2_for_add(d, s[i][j]), mul2_for_add(kk[j], rr[i]));
-          }
+          for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], rr[i], mul2(d, s[i][j]));
         }
       }
 #pragma unroll
