@@ -448,11 +448,52 @@ static_assert(kWindow * kDenseLanes == kDenseThreads, "one thread per record chu
 
 struct __align__(16) WindowDenseShared {
   float rk[kWindow][kKeys];      // record keys (fp32), u < position only
-  f2 rc[kWindow][kValues];       // (rc, rc) per record and row, u < position only
+  float rc[kWindow][kValues];    // record corrections (fp32), u < position only
   f2 d[kWindow];                 // (decay, decay), u < position only
   float ck[kRank][kKeys];        // compensator keys, rank-major (compensated boundary)
   f2 cv[kRank][kValues];         // (V, V) per rank and row
+  // Stage filled by cp.async one pass ahead of its use.
+  int8_t codes[kElements];                     // [v][k]: rows 0..63 pass 0, 64..127 pass 1
+  uint16_t raw_keys[kWindow][kKeys];           // next head's records (binary16)
+  uint16_t raw_corrections[kWindow][kValues];
+  float raw_decay[kWindow];
+  uint32_t raw_position[4];                    // positions[head][0..3]
+  float c[2][kKeys];                           // smoothing, by head parity
+  float b[2][kValues];                         // scales, by head parity
 };
+
+// This thread's share of head h's records, decays, position, smoothing and
+// scales (into parity slot `par`); one commit group per call site.
+__device__ __forceinline__ void dense_stage_head(const FoldParams& p, WindowDenseShared& sh,
+                                                 uint64_t h, int par, int t) {
+  cp_async16(reinterpret_cast<uint4*>(&sh.raw_keys[0][0]) + t,
+             reinterpret_cast<const uint4*>(p.w.record_keys + h * kWindow * kKeys) + t);
+  cp_async16(reinterpret_cast<uint4*>(&sh.raw_corrections[0][0]) + t,
+             reinterpret_cast<const uint4*>(p.w.record_corrections + h * kWindow * kValues) + t);
+  if (t < kWindow / 4) {
+    cp_async16(reinterpret_cast<float4*>(sh.raw_decay) + t,
+               reinterpret_cast<const float4*>(p.w.record_decay + h * kWindow) + t);
+  } else if (t == kWindow / 4) {
+    cp_async16(sh.raw_position, p.w.positions + h * kPositionStride);
+  } else if (t >= 32 && t < 32 + kKeys / 4) {
+    cp_async16(reinterpret_cast<float4*>(sh.c[par]) + (t - 32),
+               reinterpret_cast<const float4*>(p.w.smoothing + h * kKeys) + (t - 32));
+  } else if (t >= 64 && t < 64 + kValues / 4) {
+    cp_async16(reinterpret_cast<float4*>(sh.b[par]) + (t - 64),
+               reinterpret_cast<const float4*>(p.w.scales + h * kValues) + (t - 64));
+  }
+}
+// This thread's share of head h's codes for one pass (64 rows, 8 KiB).
+__device__ __forceinline__ void dense_stage_codes(const FoldParams& p, WindowDenseShared& sh,
+                                                  uint64_t h, int pass, int t) {
+  const uint4* src = reinterpret_cast<const uint4*>(p.w.codes + h * kElements) +
+                     pass * (kElements / 2 / 16);
+  uint4* dst = reinterpret_cast<uint4*>(sh.codes) + pass * (kElements / 2 / 16);
+  cp_async16(dst + t, src + t);
+  cp_async16(dst + t + kDenseThreads, src + t + kDenseThreads);
+}
+static_assert(kElements / 2 / 16 == 2 * kDenseThreads, "two 16-byte code chunks per thread");
+static_assert(kWindow * kKeys * 2 / 16 == kDenseThreads, "one 16-byte record chunk per thread");
 
 // a / 127 for both lanes, exact for every float (the two-term reciprocal
 // below 2^-112 is replaced by the IEEE division, as in div127_any).
@@ -484,30 +525,124 @@ __device__ __forceinline__ void dense_boundary(uint32_t zw, float4 c, bool c_saf
   s23 = mul2(q23, bb);
 }
 
+// One pass (64 rows) of this thread's tile: dequantize, compensators,
+// records, store; returns the finiteness accumulator.
+template <bool kComp>
+__device__ __forceinline__ f2 dense_pass(const WindowDenseShared& sh, int pass, int par, int np,
+                                         bool c_safe, int ka, int kb, int row0, float* rows,
+                                         f2 flags) {
+  const int v0 = pass * kDenseRowsPerPass + row0;
+  uint32_t za[kDenseRows], zb[kDenseRows];
+#pragma unroll
+  for (int i = 0; i < kDenseRows; ++i) {
+    za[i] = *reinterpret_cast<const uint32_t*>(&sh.codes[(v0 + i) * kKeys + ka]);
+    zb[i] = *reinterpret_cast<const uint32_t*>(&sh.codes[(v0 + i) * kKeys + kb]);
+  }
+  const float4 ca = *reinterpret_cast<const float4*>(&sh.c[par][ka]);
+  const float4 cb = *reinterpret_cast<const float4*>(&sh.c[par][kb]);
+  const float4 b4 = *reinterpret_cast<const float4*>(&sh.b[par][v0]);
+  const float bs[kDenseRows] = {b4.x, b4.y, b4.z, b4.w};
+  f2 s[kDenseRows][4];  // row i: keys (ka, ka+1), (ka+2, ka+3), (kb, kb+1), (kb+2, kb+3)
+#pragma unroll
+  for (int i = 0; i < kDenseRows; ++i) {
+    const f2 bb = pack2(bs[i], bs[i]);
+    dense_boundary(za[i], ca, c_safe, bb, s[i][0], s[i][1]);
+    dense_boundary(zb[i], cb, c_safe, bb, s[i][2], s[i][3]);
+  }
+  if constexpr (kComp) {  // compensators by rank: S = RN(S + RN(K[k][m] V[v][m]))
+#pragma unroll
+    for (int m = 0; m < kRank; ++m) {
+      const float4 k4a = *reinterpret_cast<const float4*>(&sh.ck[m][ka]);
+      const float4 k4b = *reinterpret_cast<const float4*>(&sh.ck[m][kb]);
+      const float4 v01 = *reinterpret_cast<const float4*>(&sh.cv[m][v0]);
+      const float4 v23 = *reinterpret_cast<const float4*>(&sh.cv[m][v0 + 2]);
+      const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
+      const f2 vv[kDenseRows] = {lo_pair(v01), hi_pair(v01), lo_pair(v23), hi_pair(v23)};
+      // K and V are binary16 too: the product is exact, so the add is one fma.
+#pragma unroll
+      for (int i = 0; i < kDenseRows; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], vv[i], s[i][j]);
+      }
+    }
+  }
+  // Records oldest first: S = RN(RN(d S) + RN(key correction)).  Key and
+  // correction are binary16 values (11-bit significands, magnitudes in
+  // [2^-24, 65504]), so their product has at most 22 significant bits and
+  // lies in fp32's normal range: RN(key correction) = key correction, and the
+  // update is exactly fma(key, correction, RN(d S)) -- two operations per
+  // element instead of three, for every input including zeros of either
+  // sign, infinities and NaN.
+#pragma unroll 8
+  for (int u = 0; u < np; ++u) {
+    const f2 d = sh.d[u];
+    const float4 k4a = *reinterpret_cast<const float4*>(&sh.rk[u][ka]);
+    const float4 k4b = *reinterpret_cast<const float4*>(&sh.rk[u][kb]);
+    const float4 r4 = *reinterpret_cast<const float4*>(&sh.rc[u][v0]);
+    const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
+    const f2 rr[kDenseRows] = {pack2(r4.x, r4.x), pack2(r4.y, r4.y), pack2(r4.z, r4.z),
+                               pack2(r4.w, r4.w)};
+#pragma unroll
+    for (int i = 0; i < kDenseRows; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], rr[i], mul2(d, s[i][j]));
+    }
+  }
+  const f2 zero = pack2(0.0F, 0.0F);
+#pragma unroll
+  for (int i = 0; i < kDenseRows; ++i) {
+    float* row = rows + (v0 + i) * kKeys;
+    __stcg(reinterpret_cast<float4*>(row + ka),
+           make_float4(lo2(s[i][0]), hi2(s[i][0]), lo2(s[i][1]), hi2(s[i][1])));
+    __stcg(reinterpret_cast<float4*>(row + kb),
+           make_float4(lo2(s[i][2]), hi2(s[i][2]), lo2(s[i][3]), hi2(s[i][3])));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) flags = fma2(s[i][j], zero, flags);
+  }
+  return flags;
+}
+
 // Four CTAs per SM (64 registers) for the quant-only boundary; the
 // compensated one keeps three so that its rank loop does not spill.
+//
+// Software pipeline per CTA (cp.async, 16-byte copies, each thread waiting
+// on its own commit groups, a block barrier publishing them): the next
+// head's records, position, smoothing and scales are staged while this
+// head's first pass runs, and each pass's 64 code rows one pass ahead.  The
+// commit groups stay in issue order: [head h + pass-0 codes], [pass-1 codes],
+// then per head [next head], [next pass-0 codes], [next pass-1 codes]
+// (empty groups past the last head keep the count uniform).
 template <bool kComp>
 __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
     window_dense_kernel(FoldParams p) {
-  __shared__ WindowDenseShared sh;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  WindowDenseShared& sh = *reinterpret_cast<WindowDenseShared*>(smem_raw);
   const int t = threadIdx.x;
   const int lane = t % kDenseLanes;
   const int ka = 4 * lane, kb = kKeys / 2 + 4 * lane;
   const int row0 = kDenseRows * (t / kDenseLanes);
-  const f2 zero = pack2(0.0F, 0.0F);
-  for (uint64_t head = blockIdx.x; head < p.heads; head += gridDim.x) {
-    const uint32_t pos_raw = __ldcg(p.w.positions + head * kPositionStride);
+  uint64_t head = blockIdx.x;
+  if (head < p.heads) {
+    dense_stage_head(p, sh, head, 0, t);
+    dense_stage_codes(p, sh, head, 0, t);
+    cp_async_commit();
+    dense_stage_codes(p, sh, head, 1, t);
+    cp_async_commit();
+  }
+  for (int par = 0; head < p.heads; head += gridDim.x, par ^= 1) {
+    const uint64_t next = head + gridDim.x;
+    const bool has_next = next < p.heads;
+    cp_async_wait<1>();  // this head's records and pass-0 codes (pass-1 codes may be in flight)
+    __syncthreads();
+    const uint32_t pos_raw = sh.raw_position[0];
     const int np = pos_raw < static_cast<uint32_t>(kWindow) ? static_cast<int>(pos_raw) : kWindow;
     const uint64_t rbase = head * kWindow;
-    const int8_t* codes = p.w.codes + head * kElements;
-    // ---- records (u < position) to shared memory: 8 keys and 8 rows a thread --
+    // ---- records (u < position) to fp32: 8 keys and 8 corrections a thread --
     {
       const int u = t / kDenseLanes, k8 = 8 * (t % kDenseLanes);
       if (u < np) {
-        const uint4 kw = __ldcg(reinterpret_cast<const uint4*>(p.w.record_keys +
-                                                               (rbase + u) * kKeys + k8));
-        const uint4 cw = __ldcg(reinterpret_cast<const uint4*>(p.w.record_corrections +
-                                                               (rbase + u) * kValues + k8));
+        const uint4 kw = *reinterpret_cast<const uint4*>(&sh.raw_keys[u][k8]);
+        const uint4 cw = *reinterpret_cast<const uint4*>(&sh.raw_corrections[u][k8]);
         const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
         const uint32_t cws[4] = {cw.x, cw.y, cw.z, cw.w};
         float4* rk = reinterpret_cast<float4*>(&sh.rk[u][k8]);
@@ -517,17 +652,12 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
           rk[j] = make_float4(half_to_float(kws[2 * j] & 0xFFFFu), half_to_float(kws[2 * j] >> 16),
                               half_to_float(kws[2 * j + 1] & 0xFFFFu),
                               half_to_float(kws[2 * j + 1] >> 16));
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = half_to_float(cws[j] & 0xFFFFu), hi = half_to_float(cws[j] >> 16);
-          rc[j] = make_float4(lo, lo, hi, hi);
+          rc[j] = make_float4(half_to_float(cws[2 * j] & 0xFFFFu), half_to_float(cws[2 * j] >> 16),
+                              half_to_float(cws[2 * j + 1] & 0xFFFFu),
+                              half_to_float(cws[2 * j + 1] >> 16));
         }
       }
-      if (t < np) {
-        const float d = __ldcg(p.w.record_decay + rbase + t);
-        sh.d[t] = pack2(d, d);
-      }
+      if (t < np) sh.d[t] = pack2(sh.raw_decay[t], sh.raw_decay[t]);
     }
     if constexpr (kComp) {
       if (t < kKeys) {
@@ -545,7 +675,9 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
         for (int m = 0; m < kRank; ++m) sh.cv[m][v] = pack2(vm[m], vm[m]);
       }
     }
-    __syncthreads();
+    __syncthreads();  // converted records visible; the record stage is free
+    if (has_next) dense_stage_head(p, sh, next, par ^ 1, t);
+    cp_async_commit();
     // ---- the window is about to be folded: clear it ------------------------
     {
       const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
@@ -566,8 +698,8 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
     // otherwise each product is checked.
     bool c_safe = true;
     {
-      const float4 ca = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + ka));
-      const float4 cb = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + kb));
+      const float4 ca = *reinterpret_cast<const float4*>(&sh.c[par][ka]);
+      const float4 cb = *reinterpret_cast<const float4*>(&sh.c[par][kb]);
       const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -576,85 +708,22 @@ __global__ void __launch_bounds__(kDenseThreads, kComp ? 3 : 4)
     }
     // x * 0 + flags stays +0 while every element is finite and becomes NaN
     // otherwise (x * 0 is NaN exactly for infinite or NaN x).
-    f2 flags = zero;
     float* rows = p.workspace + head * kElements;
-#pragma unroll 1
-    for (int pass = 0; pass < kDensePasses; ++pass) {
-      const int v0 = pass * kDenseRowsPerPass + row0;
-      uint32_t za[kDenseRows], zb[kDenseRows];
-#pragma unroll
-      for (int i = 0; i < kDenseRows; ++i) {
-        za[i] = ld_cs_u32(codes + (v0 + i) * kKeys + ka);
-        zb[i] = ld_cs_u32(codes + (v0 + i) * kKeys + kb);
-      }
-      // Smoothing reloaded per pass (a cache hit) rather than held across it.
-      const float4 ca = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + ka));
-      const float4 cb = __ldg(reinterpret_cast<const float4*>(p.w.smoothing + head * kKeys + kb));
-      const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.w.scales + head * kValues + v0));
-      const float bs[kDenseRows] = {b4.x, b4.y, b4.z, b4.w};
-      f2 s[kDenseRows][4];  // row i: keys (ka, ka+1), (ka+2, ka+3), (kb, kb+1), (kb+2, kb+3)
-#pragma unroll
-      for (int i = 0; i < kDenseRows; ++i) {
-        const f2 bb = pack2(bs[i], bs[i]);
-        dense_boundary(za[i], ca, c_safe, bb, s[i][0], s[i][1]);
-        dense_boundary(zb[i], cb, c_safe, bb, s[i][2], s[i][3]);
-      }
-      if constexpr (kComp) {  // compensators by rank: S = RN(S + RN(K[k][m] V[v][m]))
-#pragma unroll
-        for (int m = 0; m < kRank; ++m) {
-          const float4 k4a = *reinterpret_cast<const float4*>(&sh.ck[m][ka]);
-          const float4 k4b = *reinterpret_cast<const float4*>(&sh.ck[m][kb]);
-          const float4 v01 = *reinterpret_cast<const float4*>(&sh.cv[m][v0]);
-          const float4 v23 = *reinterpret_cast<const float4*>(&sh.cv[m][v0 + 2]);
-          const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
-          const f2 vv[kDenseRows] = {lo_pair(v01), hi_pair(v01), lo_pair(v23), hi_pair(v23)};
-          // K and V are binary16 too: the product is exact, so the add is
-          // one fma.
-#pragma unroll
-          for (int i = 0; i < kDenseRows; ++i) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], vv[i], s[i][j]);
-          }
-        }
-      }
-      // Records oldest first: S = RN(RN(d S) + RN(key correction)).  Key and
-      // correction are binary16 values (11-bit significands, magnitudes in
-      // [2^-24, 65504]), so their product has at most 22 significant bits and
-      // lies in fp32's normal range: RN(key correction) = key correction,
-      // and the update is exactly fma(key, correction, RN(d S)) -- two
-      // operations per element instead of three, for every input including
-      // zeros of either sign, infinities and NaN.
-#pragma unroll 8
-      for (int u = 0; u < np; ++u) {
-        const f2 d = sh.d[u];
-        const float4 k4a = *reinterpret_cast<const float4*>(&sh.rk[u][ka]);
-        const float4 k4b = *reinterpret_cast<const float4*>(&sh.rk[u][kb]);
-        const float4 r01 = *reinterpret_cast<const float4*>(&sh.rc[u][v0]);
-        const float4 r23 = *reinterpret_cast<const float4*>(&sh.rc[u][v0 + 2]);
-        const f2 kk[4] = {lo_pair(k4a), hi_pair(k4a), lo_pair(k4b), hi_pair(k4b)};
-        const f2 rr[kDenseRows] = {lo_pair(r01), hi_pair(r01), lo_pair(r23), hi_pair(r23)};
-#pragma unroll
-        for (int i = 0; i < kDenseRows; ++i) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) s[i][j] = fma2(kk[j], rr[i], mul2(d, s[i][j]));
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kDenseRows; ++i) {
-        float* row = rows + (v0 + i) * kKeys;
-        __stcg(reinterpret_cast<float4*>(row + ka),
-               make_float4(lo2(s[i][0]), hi2(s[i][0]), lo2(s[i][1]), hi2(s[i][1])));
-        __stcg(reinterpret_cast<float4*>(row + kb),
-               make_float4(lo2(s[i][2]), hi2(s[i][2]), lo2(s[i][3]), hi2(s[i][3])));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) flags = fma2(s[i][j], zero, flags);
-      }
-    }
+    f2 flags = dense_pass<kComp>(sh, 0, par, np, c_safe, ka, kb, row0, rows, pack2(0.0F, 0.0F));
+    cp_async_wait<1>();  // this head's pass-1 codes (the next head's records may be in flight)
+    __syncthreads();     // pass 0 done everywhere: its code rows are free
+    if (has_next) dense_stage_codes(p, sh, next, 0, t);
+    cp_async_commit();
+    flags = dense_pass<kComp>(sh, 1, par, np, c_safe, ka, kb, row0, rows, flags);
     const bool finite = lo2(flags) == 0.0F && hi2(flags) == 0.0F;
-    // Also the barrier before the next head's records overwrite shared memory.
+    // Also the barrier before pass-1 code rows and shared memory are reused.
     if (__syncthreads_or(!finite) != 0 && t == 0) report(nullptr, kStatusWindowNonFinite);
+    if (has_next) dense_stage_codes(p, sh, next, 1, t);
+    cp_async_commit();
   }
 }
+
+inline size_t window_dense_smem_bytes() { return sizeof(WindowDenseShared); }
 
 inline size_t window_fold_smem_bytes() {
   return ((sizeof(FitShared) + 15) & ~size_t{15}) + sizeof(FoldExtra);
@@ -809,11 +878,18 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->fold, window_fold_kernel, kFitThreads,
                                                       window_fold_smem_bytes());
   if (err != cudaSuccess) return err;
+  const int dense_smem = static_cast<int>(window_dense_smem_bytes());
+  err = cudaFuncSetAttribute(window_dense_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dense_smem);
+  if (err != cudaSuccess) return err;
+  err = cudaFuncSetAttribute(window_dense_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dense_smem);
+  if (err != cudaSuccess) return err;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense[0], window_dense_kernel<false>,
-                                                      kDenseThreads, 0);
+                                                      kDenseThreads, dense_smem);
   if (err != cudaSuccess) return err;
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->window_dense[1], window_dense_kernel<true>,
-                                                      kDenseThreads, 0);
+                                                      kDenseThreads, dense_smem);
   if (err != cudaSuccess) return err;
   err = cudaFuncSetAttribute(dense_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(sizeof(DenseStepShared)));
@@ -848,10 +924,11 @@ inline cudaError_t launch_window_fold(const FoldParams& p, int grid, cudaStream_
 }
 
 inline cudaError_t launch_window_dense(const FoldParams& p, int grid, cudaStream_t stream) {
+  const size_t smem = window_dense_smem_bytes();
   if (p.w.ck != nullptr) {
-    window_dense_kernel<true><<<grid, kDenseThreads, 0, stream>>>(p);
+    window_dense_kernel<true><<<grid, kDenseThreads, smem, stream>>>(p);
   } else {
-    window_dense_kernel<false><<<grid, kDenseThreads, 0, stream>>>(p);
+    window_dense_kernel<false><<<grid, kDenseThreads, smem, stream>>>(p);
   }
   return cudaGetLastError();
 }
