@@ -88,7 +88,7 @@ const DeviceSetup* device_setup() {
   if (prepare_window(&s.window) != cudaSuccess || s.window.fold < 1 || s.window.dense < 1 ||
       s.window.window_dense[0] < 1 || s.window.window_dense[1] < 1 ||
       s.window.step[0][0] < 1 || s.window.step[0][1] < 1 || s.window.step[1][0] < 1 ||
-      s.window.step[1][1] < 1) {
+      s.window.step[1][1] < 1 || s.window.step_staged[0] < 1 || s.window.step_staged[1] < 1) {
     return nullptr;
   }
   s.ready = true;
@@ -669,6 +669,16 @@ bool window_ok(const WindowBuffers& w, bool need_compensators) {
 int32_t run_window_step(void* stream, bool qwen, bool comp, const StepParams& p) {
   const DeviceSetup* s = device_setup();
   if (s == nullptr) return kSetupFailed;
+  // The staged Qwen step copies key, query and value rows and the beta pair
+  // with cp.async: 16-byte aligned rows and a 4-byte aligned beta.
+  if (qwen && aligned16(p.keys) && aligned16(p.queries) && aligned16(p.values) &&
+      aligned4(p.beta)) {
+    const int grid = grid_for(p.heads, s->sms, s->window.step_staged[comp]);
+    return launch_window_step_staged(comp, p, grid, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? kOk
+               : kLaunchFailed;
+  }
   const int grid = grid_for(p.heads, s->sms, s->window.step[qwen][comp]);
   return launch_window_step(qwen, comp, p, grid, static_cast<cudaStream_t>(stream)) ==
                  cudaSuccess

@@ -38,6 +38,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include "codec_device.cuh"
@@ -320,6 +321,293 @@ __global__ void __launch_bounds__(kWinThreads, 6) window_step_kernel(StepParams 
 template <bool kQwen>
 inline size_t window_step_smem_bytes() {
   return kQwen ? sizeof(StepShared) : sizeof(StepSharedCapsule);
+}
+
+// ---------------------------------------------------------------------------
+// Qwen3.5 step with the next head's inputs staged a head ahead.  The same
+// arithmetic as window_step_kernel<true, kComp>; every per-head global read
+// (codes, records, position, smoothing, scales, compensators and the token's
+// log decay, beta, key, query and value) is a cp.async into one stage that
+// the CTA consumes at the start of the head -- codes into registers, records
+// converted into the chain rows -- and then refills for its next head while
+// this head's suffix, chains and readout run.  Four CTAs per SM (55 KB of
+// shared memory each) for a quant-only boundary, three with compensators.
+// Needs 16-byte aligned key, query and value rows and a 4-byte aligned beta
+// (the host checks and otherwise launches window_step_kernel).
+
+struct __align__(16) StepStage {
+  uint4 codes[kValues][8];          // provider row v, 16-byte chunk j at j ^ (v & 7)
+  uint16_t rkeys[kWindow][kKeys];   // records (binary16)
+  uint16_t rcorr[kWindow][kValues];
+  float rdecay[kWindow];
+  uint32_t position[4];             // positions[head][0..3]
+  float c[kKeys];                   // smoothing
+  float b[kValues];                 // scales
+  uint16_t key[kKeys];              // bf16 token inputs of the head
+  uint16_t query[kKeys];
+  uint16_t value[kValues];
+  float log_decay;
+  uint32_t beta_pair;               // beta[head & ~1], beta[head | 1]
+  uint32_t pad[2];
+};
+
+struct __align__(16) StagedComp {
+  float4 ck[kKeys];                 // compensator keys (fp32) for the chains
+  uint2 stage_ck[kKeys];            // staged binary16 compensators
+  uint2 stage_cv[kValues];
+};
+struct StagedNoComp {};
+
+// The step's working set (as StepShared, without the compensator keys of a
+// quant-only boundary) and the stage: 55 KB quant-only, four CTAs per SM.
+template <bool kComp>
+struct __align__(16) StagedStepShared {
+  float suffix[2][kWindow][kRowPad];
+  float rkey[kWindow][kRowPad];
+  float4 sq[kKeys / 2];
+  float c[kKeys];
+  float key[kKeys];
+  float query[kKeys];
+  float proj[2][kWindow];
+  float cproj[2][kRank];
+  float rdecay[kWindow];
+  float up;
+  StepStage stage;
+  typename std::conditional<kComp, StagedComp, StagedNoComp>::type comp;
+};
+
+// This thread's share of head h's stage (all 128 threads issue; one commit).
+template <bool kComp, class Shared>
+__device__ __forceinline__ void step_stage_issue(const StepParams& p, Shared& sh, uint64_t h,
+                                                 int t) {
+  StepStage& st = sh.stage;
+  const uint4* codes = reinterpret_cast<const uint4*>(p.w.codes + h * kElements);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int i = t + kWinThreads * m;  // chunk j of row v, read coalesced
+    const int v = i >> 3, j = i & 7;
+    cp_async16(&st.codes[v][j ^ (v & 7)], codes + i);
+  }
+  // records: 2 x 4 KiB = 512 chunks, 4 per thread
+  cp_async16(reinterpret_cast<uint4*>(&st.rkeys[0][0]) + t,
+             reinterpret_cast<const uint4*>(p.w.record_keys + h * kWindow * kKeys) + t);
+  cp_async16(reinterpret_cast<uint4*>(&st.rkeys[0][0]) + t + kWinThreads,
+             reinterpret_cast<const uint4*>(p.w.record_keys + h * kWindow * kKeys) + t + kWinThreads);
+  cp_async16(reinterpret_cast<uint4*>(&st.rcorr[0][0]) + t,
+             reinterpret_cast<const uint4*>(p.w.record_corrections + h * kWindow * kValues) + t);
+  cp_async16(reinterpret_cast<uint4*>(&st.rcorr[0][0]) + t + kWinThreads,
+             reinterpret_cast<const uint4*>(p.w.record_corrections + h * kWindow * kValues) + t +
+                 kWinThreads);
+  if (t < 4) {
+    cp_async16(reinterpret_cast<uint4*>(st.rdecay) + t,
+               reinterpret_cast<const uint4*>(p.w.record_decay + h * kWindow) + t);
+  } else if (t == 4) {
+    cp_async16(st.position, p.w.positions + h * kPositionStride);
+  } else if (t == 5) {
+    cp_async4(&st.log_decay, p.decay + h);
+  } else if (t == 6) {
+    cp_async4(&st.beta_pair, p.beta + (h & ~uint64_t{1}));
+  } else if (t >= 32 && t < 64) {
+    const int i = t - 32;
+    cp_async16(reinterpret_cast<uint4*>(st.c) + i,
+               reinterpret_cast<const uint4*>(p.w.smoothing + h * kKeys) + i);
+  } else if (t >= 64 && t < 96) {
+    const int i = t - 64;
+    cp_async16(reinterpret_cast<uint4*>(st.b) + i,
+               reinterpret_cast<const uint4*>(p.w.scales + h * kValues) + i);
+  } else if (t >= 96) {
+    const int i = t - 96;  // 32 threads: key, query (16 chunks each)
+    const uint4* kq = reinterpret_cast<const uint4*>(i < 16 ? p.keys : p.queries) +
+                      (h >> 1) * (kKeys / 8);
+    cp_async16(reinterpret_cast<uint4*>(i < 16 ? st.key : st.query) + (i & 15), kq + (i & 15));
+  }
+  if (t >= 7 && t < 7 + 16) {
+    const int i = t - 7;
+    cp_async16(reinterpret_cast<uint4*>(st.value) + i,
+               reinterpret_cast<const uint4*>(p.values + h * kValues) + i);
+  }
+  if constexpr (kComp) {
+    // 2 x 1 KiB = 128 chunks, one per thread
+    if (t < 64) {
+      cp_async16(reinterpret_cast<uint4*>(sh.comp.stage_ck) + t,
+                 reinterpret_cast<const uint4*>(p.w.ck + h * kKeys * kRank) + t);
+    } else {
+      cp_async16(reinterpret_cast<uint4*>(sh.comp.stage_cv) + (t - 64),
+                 reinterpret_cast<const uint4*>(p.w.cv + h * kValues * kRank) + (t - 64));
+    }
+  }
+  cp_async_commit();
+}
+
+template <bool kComp>
+__global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
+    window_step_staged_kernel(StepParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  StagedStepShared<kComp>& sh = *reinterpret_cast<StagedStepShared<kComp>*>(smem_raw);
+  StepStage& st = sh.stage;
+  const int t = threadIdx.x;
+  uint64_t head = blockIdx.x;
+  if (head < p.heads) step_stage_issue<kComp>(p, sh, head, t);
+  for (; head < p.heads; head += gridDim.x) {
+    const uint64_t next = head + gridDim.x;
+    cp_async_wait<0>();
+    __syncthreads();  // this head's stage has landed; the previous head is done
+    const uint32_t pos = st.position[0];
+    const uint64_t rbase = head * kWindow;
+    if (pos >= kWindow) {  // block-uniform: every thread read the same word
+      if (t == 0) report(nullptr, kStatusWindowFull);
+      __syncthreads();  // every thread has read the stage
+      if (next < p.heads) step_stage_issue<kComp>(p, sh, next, t);
+      continue;
+    }
+    const int np = static_cast<int>(pos);
+    // ---- consume the stage: codes row t to registers, records, inputs -------
+    uint4 zrow[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) zrow[j] = st.codes[t][j ^ (t & 7)];
+    const float alpha = expf(st.log_decay);
+    const float beta = bf16_to_float(static_cast<uint16_t>(st.beta_pair >> (16 * (head & 1))));
+    const float k = bf16_to_float(st.key[t]);
+    const float key_t = __fmul_rn(beta, k);
+    const float read_t = __fmul_rn(alpha, k);
+    const float query_t = __fmul_rn(kQueryScale, bf16_to_float(st.query[t]));
+    const float value_t = bf16_to_float(st.value[t]);
+    sh.key[t] = key_t;
+    sh.query[t] = query_t;
+    sh.c[t] = st.c[t];
+    const float b_t = st.b[t];
+    float cv_t[kRank] = {0.F, 0.F, 0.F, 0.F};
+    if constexpr (kComp) {
+      const uint2 kw = sh.comp.stage_ck[t];
+      sh.comp.ck[t] = make_float4(half_to_float(kw.x & 0xFFFFu), half_to_float(kw.x >> 16),
+                                  half_to_float(kw.y & 0xFFFFu), half_to_float(kw.y >> 16));
+      const uint2 vw = sh.comp.stage_cv[t];
+      cv_t[0] = half_to_float(vw.x & 0xFFFFu);
+      cv_t[1] = half_to_float(vw.x >> 16);
+      cv_t[2] = half_to_float(vw.y & 0xFFFFu);
+      cv_t[3] = half_to_float(vw.y >> 16);
+    }
+    if (t < kWindow) sh.rdecay[t] = st.rdecay[t];
+    float rc[kWindow];
+#pragma unroll
+    for (int u = 0; u < kWindow; ++u) {
+      sh.rkey[u][t] = half_to_float(st.rkeys[u][t]);
+      rc[u] = half_to_float(st.rcorr[u][t]);
+    }
+    __syncthreads();  // the stage is consumed: refill it with the next head
+    if (next < p.heads) step_stage_issue<kComp>(p, sh, next, t);
+    // ---- suffix-decayed read and query (thread t = key t) -----------------
+    {
+      float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
+#pragma unroll
+      for (int u = kWindow - 1; u >= 0; --u) {  // record u is read with suffix np-1-u
+        if (u < np) {
+          sh.suffix[0][np - 1 - u][t] = s0;
+          sh.suffix[1][np - 1 - u][t] = s1;
+          const float d = sh.rdecay[u];
+          s0 = __fmul_rn(s0, d);
+          s1 = __fmul_rn(s1, d);
+        }
+      }
+      float* sq = reinterpret_cast<float*>(sh.sq) + 4 * (t >> 1) + (t & 1);
+      sq[0] = s0;
+      sq[2] = s1;
+    }
+    __syncthreads();
+    // ---- sequential projections: records, compensators, update -----------
+    const int chains = 2 * np + (kComp ? 2 * kRank : 0) + 1;
+    bool comp_chain = false;
+    if constexpr (kComp) {
+      comp_chain = t >= 2 * np && t < 2 * np + 2 * kRank;
+      if (comp_chain) {
+        const int i = t - 2 * np;
+        const int r = i / kRank, m = i % kRank;
+        const float* ck = reinterpret_cast<const float*>(sh.comp.ck) + m;
+        const float* sq = reinterpret_cast<const float*>(sh.sq) + 2 * r;
+        float acc = 0.0F;
+#pragma unroll 8
+        for (int kk = 0; kk < kKeys; ++kk) {
+          acc = __fadd_rn(acc, __fmul_rn(ck[4 * kk], sq[4 * (kk >> 1) + (kk & 1)]));
+        }
+        sh.cproj[r][m] = acc;
+      }
+    }
+    if (!comp_chain && t < chains) {
+      const float* a = sh.key;
+      const float* bq = sh.query;
+      float* dst = &sh.up;
+      if (t < 2 * np) {
+        const int r = t / np == 0 ? 0 : 1;
+        const int u = t - r * np;
+        a = &sh.rkey[u][0];
+        bq = &sh.suffix[r][np - 1 - u][0];
+        dst = &sh.proj[r][u];
+      }
+      *dst = chain_dot4(a, bq);
+    }
+    // ---- boundary readout of column t for both reads ----------------------
+    float acc0 = 0.0F, acc1 = 0.0F;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t words[4] = {zrow[i].x, zrow[i].y, zrow[i].z, zrow[i].w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int k0 = 16 * i + 4 * w;
+        f2 z01, z23;
+        unpack_codes(words[w], z01, z23);
+        const float4 c4 = *reinterpret_cast<const float4*>(&sh.c[k0]);
+        const f2 zc01 = mul2(z01, pack2(c4.x, c4.y));
+        const f2 zc23 = mul2(z23, pack2(c4.z, c4.w));
+        const float4 sa = sh.sq[k0 >> 1], sb = sh.sq[(k0 >> 1) + 1];
+        f2 p0 = mul2_for_add(zc01, pack2(sa.x, sa.y));
+        f2 p1 = mul2_for_add(zc01, pack2(sa.z, sa.w));
+        acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+        acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
+        p0 = mul2_for_add(zc23, pack2(sb.x, sb.y));
+        p1 = mul2_for_add(zc23, pack2(sb.z, sb.w));
+        acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+        acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
+      }
+    }
+    __syncthreads();
+    // ---- column t: records newest first, boundary, compensators -----------
+    float out0 = 0.0F, out1 = 0.0F;
+#pragma unroll
+    for (int u = kWindow - 1; u >= 0; --u) {
+      if (u < np) {
+        out0 = __fadd_rn(out0, __fmul_rn(rc[u], sh.proj[0][u]));
+        out1 = __fadd_rn(out1, __fmul_rn(rc[u], sh.proj[1][u]));
+      }
+    }
+    out0 = __fadd_rn(out0, __fmul_rn(div127_any(acc0), b_t));
+    out1 = __fadd_rn(out1, __fmul_rn(div127_any(acc1), b_t));
+    if constexpr (kComp) {
+#pragma unroll
+      for (int m = 0; m < kRank; ++m) {
+        out0 = __fadd_rn(out0, __fmul_rn(cv_t[m], sh.cproj[0][m]));
+        out1 = __fadd_rn(out1, __fmul_rn(cv_t[m], sh.cproj[1][m]));
+      }
+    }
+    const float correction = __fsub_rn(value_t, out0);
+    const float output = __fadd_rn(out1, __fmul_rn(correction, sh.up));
+    static_cast<uint16_t*>(p.outputs)[head * kValues + t] =
+        __bfloat16_as_ushort(__float2bfloat16_rn(output));
+    if (!isfinite(output)) report(nullptr, kStatusWindowNonFinite);
+    // ---- append the record -------------------------------------------------
+    p.w.record_keys[(rbase + np) * kKeys + t] = float_to_half_bits(key_t);
+    p.w.record_corrections[(rbase + np) * kValues + t] = float_to_half_bits(correction);
+    if (t == 0) {
+      p.w.record_decay[rbase + np] = alpha;
+      p.w.positions[head * kPositionStride] = pos + 1u;
+    }
+    // The barrier at the top of the next head orders these shared-memory
+    // reads before the next head's writes.
+  }
+}
+
+template <bool kComp>
+inline size_t window_step_staged_smem_bytes() {
+  return sizeof(StagedStepShared<kComp>);
 }
 
 // ---------------------------------------------------------------------------
@@ -851,6 +1139,7 @@ __global__ void __launch_bounds__(kWinThreads, kDenseStepBlocksPerSm)
 
 struct WindowBlocks {
   int step[2][2] = {};  // [qwen][comp] blocks per SM
+  int step_staged[2] = {};  // [comp]
   int fold = 0;
   int window_dense[2] = {};  // [compensated]
   int dense = 0;
@@ -866,8 +1155,20 @@ inline cudaError_t prepare_step_variant(int* blocks) {
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, kWinThreads, smem);
 }
 
+template <bool kComp>
+inline cudaError_t prepare_staged_variant(int* blocks) {
+  const auto kernel = window_step_staged_kernel<kComp>;
+  const size_t smem = window_step_staged_smem_bytes<kComp>();
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, kWinThreads, smem);
+}
+
 inline cudaError_t prepare_window(WindowBlocks* b) {
   cudaError_t err;
+  if ((err = prepare_staged_variant<false>(&b->step_staged[0])) != cudaSuccess) return err;
+  if ((err = prepare_staged_variant<true>(&b->step_staged[1])) != cudaSuccess) return err;
   if ((err = prepare_step_variant<true, true>(&b->step[1][1])) != cudaSuccess) return err;
   if ((err = prepare_step_variant<true, false>(&b->step[1][0])) != cudaSuccess) return err;
   if ((err = prepare_step_variant<false, true>(&b->step[0][1])) != cudaSuccess) return err;
@@ -896,6 +1197,20 @@ inline cudaError_t prepare_window(WindowBlocks* b) {
   if (err != cudaSuccess) return err;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b->dense, dense_step_kernel, kWinThreads,
                                                        sizeof(DenseStepShared));
+}
+
+inline cudaError_t launch_window_step_staged(bool comp, const StepParams& p, int grid,
+                                             cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWinThreads);
+  cfg.stream = stream;
+  if (comp) {
+    cfg.dynamicSmemBytes = window_step_staged_smem_bytes<true>();
+    return cudaLaunchKernelEx(&cfg, window_step_staged_kernel<true>, p);
+  }
+  cfg.dynamicSmemBytes = window_step_staged_smem_bytes<false>();
+  return cudaLaunchKernelEx(&cfg, window_step_staged_kernel<false>, p);
 }
 
 inline cudaError_t launch_window_step(bool qwen, bool comp, const StepParams& p, int grid,

@@ -36,6 +36,18 @@ def f32_dev(x) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(DEV)
 
 
+def bf16_dev_shifted(bits16) -> torch.Tensor:
+    """The same bf16 values one element past an aligned address: rows only
+    2-byte aligned, which the staged step cannot copy, so the launch takes
+    the unstaged kernel."""
+    host = torch.from_numpy(np.ascontiguousarray(bits16)).view(torch.bfloat16)
+    buf = torch.empty(host.numel() + 1, dtype=torch.bfloat16, device=DEV)
+    view = buf[1:].view(host.shape)
+    view.copy_(host)
+    assert view.data_ptr() % 16 == 2
+    return view
+
+
 def window_from_case(case, layout, compensators=True) -> codec.WindowStates:
     codes = case["codes"] if layout == "capsule" else np.ascontiguousarray(
         case["codes"].transpose(0, 2, 1))
@@ -134,11 +146,16 @@ def _assert_boundary(window, heads, what):
             assert np.array_equal(bits(cv), bits(h.cv)), f"{what} head {i} compensator values"
 
 
-@pytest.mark.parametrize("full, iterations", [(False, 0), (True, 32), (True, 4)])
-def test_qwen_decode_sequence_with_refit_matches_oracle(full, iterations):
+@pytest.mark.parametrize("full, iterations, staged", [(False, 0, True), (True, 32, True),
+                                                      (True, 4, True), (False, 0, False),
+                                                      (True, 4, False)])
+def test_qwen_decode_sequence_with_refit_matches_oracle(full, iterations, staged):
     """20 Qwen3.5 tokens over 16 value heads: bf16 outputs, records and the
-    refit boundary after token 16 bit-identical to the oracle."""
+    refit boundary after token 16 bit-identical to the oracle.  `staged`:
+    16-byte aligned token rows (the staged step kernel); otherwise rows only
+    2-byte aligned (the unstaged kernel)."""
     nheads, tokens = 16, 20
+    tok = bf16_dev if staged else bf16_dev_shifted
     window = _qwen_boundary(nheads, full, seed=31 + iterations)
     heads = _oracle_heads(window)
     if not full:
@@ -153,8 +170,8 @@ def test_qwen_decode_sequence_with_refit_matches_oracle(full, iterations):
             _assert_boundary(window, heads, f"refit ({iterations} iterations)")
             check_records(window, heads, "after refit")
         out = codec.window_step_bf16(window, f32_dev(inputs["log_decay"][t]),
-                                     bf16_dev(inputs["beta"][t]), bf16_dev(inputs["keys"][t]),
-                                     bf16_dev(inputs["queries"][t]), bf16_dev(inputs["values"][t]))
+                                     tok(inputs["beta"][t]), tok(inputs["keys"][t]),
+                                     tok(inputs["queries"][t]), tok(inputs["values"][t]))
         torch.cuda.synchronize()
         pos = heads[0].position.value
         alpha = window.record_decay[:, pos].cpu().numpy()
