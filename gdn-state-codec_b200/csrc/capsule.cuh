@@ -170,6 +170,55 @@ __host__ __device__ __forceinline__ void sha256_block(uint32_t h[8], const uint3
   h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
 }
 
+// Device compression with the 32-bit adds issued as multiply-adds by a
+// runtime 1 (c_fma_one, set by prepare_capsule, so the compiler cannot fold
+// it back into an add): the adds then run on the FMA pipe beside the rotates
+// and logic operations, which alone fill the integer ALU pipe.
+__constant__ uint32_t c_fma_one;
+
+__device__ __forceinline__ uint32_t add_on_fma(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(c_fma_one), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ void sha256_block_dev(uint32_t h[8], const uint32_t block[16]) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = block[i];
+  uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+#pragma unroll
+  for (int t = 0; t < 64; ++t) {
+    uint32_t wt;
+    if (t < 16) {
+      wt = w[t];
+    } else {
+      const uint32_t w15 = w[(t - 15) & 15], w2 = w[(t - 2) & 15];
+      const uint32_t s0 = rotr32(w15, 7) ^ rotr32(w15, 18) ^ (w15 >> 3);
+      const uint32_t s1 = rotr32(w2, 17) ^ rotr32(w2, 19) ^ (w2 >> 10);
+      wt = add_on_fma(add_on_fma(add_on_fma(w[t & 15], s0), w[(t - 7) & 15]), s1);
+      w[t & 15] = wt;
+    }
+    const uint32_t big1 = rotr32(e, 6) ^ rotr32(e, 11) ^ rotr32(e, 25);
+    const uint32_t ch = (e & f) ^ (~e & g);
+    // The terms known early (h, K, W) first, the ones that wait on e last.
+    const uint32_t t1 =
+        add_on_fma(add_on_fma(add_on_fma(add_on_fma(hh, sha256_k(t)), wt), ch), big1);
+    const uint32_t big0 = rotr32(a, 2) ^ rotr32(a, 13) ^ rotr32(a, 22);
+    const uint32_t maj = (a & b) ^ (a & c) ^ (b & c);
+    hh = g;
+    g = f;
+    f = e;
+    e = add_on_fma(d, t1);
+    d = c;
+    c = b;
+    b = a;
+    a = add_on_fma(add_on_fma(t1, maj), big0);
+  }
+  h[0] += a; h[1] += b; h[2] += c; h[3] += d;
+  h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
+}
+
 __host__ __device__ __forceinline__ uint32_t load_be32(const uint8_t* p) {
   return (static_cast<uint32_t>(p[0]) << 24) | (static_cast<uint32_t>(p[1]) << 16) |
          (static_cast<uint32_t>(p[2]) << 8) | static_cast<uint32_t>(p[3]);
@@ -223,7 +272,7 @@ __device__ inline void sha256_aligned8(const uint8_t* data, uint64_t size, uint3
 #pragma unroll
       for (int i = 0; i < 8; ++i) next[i] = words[i];
     }
-    sha256_block(h, block);
+    sha256_block_dev(h, block);
   }
   uint8_t tail[128];
   const int rest = static_cast<int>(size - done);
@@ -235,7 +284,7 @@ __device__ inline void sha256_aligned8(const uint8_t* data, uint64_t size, uint3
   for (int i = 0; i < 8; ++i) tail[64 * blocks - 1 - i] = static_cast<uint8_t>(bits >> (8 * i));
   for (int b = 0; b < blocks; ++b) {
     for (int i = 0; i < 16; ++i) block[i] = load_be32(tail + 64 * b + 4 * i);
-    sha256_block(h, block);
+    sha256_block_dev(h, block);
   }
 }
 
@@ -543,6 +592,9 @@ __global__ void __launch_bounds__(kCapsuleThreads) capsule_payload_kernel(Restor
 inline cudaError_t prepare_capsule() {
   const Sha256Constants& c = sha256_constants();
   cudaError_t err = cudaMemcpyToSymbol(c_sha256_k, c.k, sizeof(c.k));
+  if (err != cudaSuccess) return err;
+  const uint32_t one = 1u;
+  err = cudaMemcpyToSymbol(c_fma_one, &one, sizeof(one));
   if (err != cudaSuccess) return err;
   return cudaMemcpyToSymbol(c_sha256_h0, c.h0, sizeof(c.h0));
 }
