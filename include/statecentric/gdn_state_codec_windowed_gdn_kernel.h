@@ -68,7 +68,10 @@ int32_t statecentric_gdn_state_codec_windowed_gdn_step_launch_v1(
  * [states/2][128] bf16 (value heads 2j and 2j+1 share query/key head j),
  * values [states][128] bf16, outputs [states][128] bf16.  key = beta k,
  * read = exp(decay) k, query = 128^-0.5 q.  states must be even; codes
- * [value][key]; compensators required. */
+ * [value][key]; compensators required.  Key, query and value rows that are
+ * 16-byte aligned and a 4-byte aligned beta take the kernel that stages each
+ * head's inputs one head ahead; other alignments (2 bytes suffice) take a
+ * kernel that loads them directly, with identical results. */
 int32_t statecentric_gdn_state_codec_windowed_gdn_step_bf16_launch_v1(
     void* stream, const int8_t* residual, const float* smoothing,
     const float* scales, const uint16_t* compensator_keys,
