@@ -188,6 +188,61 @@ def test_qwen_decode_sequence_with_refit_matches_oracle(full, iterations, staged
         check_records(window, heads, f"token {t}")
 
 
+@pytest.mark.parametrize("full", [False, True])
+def test_decode_and_refit_with_more_heads_than_resident_ctas(full):
+    """1,536 value heads (more than the 592 CTAs a B200 keeps resident), so
+    every CTA of the staged step and of the pipelined quant-only refit takes
+    several heads through its one-ahead stage: 18 tokens with a refit after
+    token 16, a seeded sample of 40 heads (both halves of the range) checked
+    bit for bit against the oracle, and every head's record state against the
+    sampled heads' oracle at the end."""
+    nheads, tokens = 1536, 18
+    window = _qwen_boundary(nheads, full, seed=91)
+    rng = np.random.default_rng(92)
+    sample = np.sort(np.concatenate([rng.choice(592, 20, replace=False),
+                                     592 + rng.choice(nheads - 592, 20, replace=False)]))
+    torch.cuda.synchronize()
+    enc = window.encoded
+    codes = enc.codes.cpu().numpy()
+    c, b = enc.smoothing.cpu().numpy(), enc.scales.cpu().numpy()
+    ck = None if not full else window.compensator_keys.float().cpu().numpy()
+    cv = None if not full else window.compensator_values.float().cpu().numpy()
+    heads = {int(i): oracle.WindowHead(codes[i], c[i], b[i], None if ck is None else ck[i],
+                                       None if cv is None else cv[i], layout="provider")
+             for i in sample}
+    inputs = wc.qwen_tokens(nheads, tokens, seed=93)
+    for t in range(tokens):
+        if t == wc.WINDOW:
+            window = codec.window_refit(window, 0)
+            torch.cuda.synchronize()
+            nz = window.encoded.codes.cpu().numpy()
+            nc = window.encoded.smoothing.cpu().numpy()
+            nb = window.encoded.scales.cpu().numpy()
+            for i, h in heads.items():
+                assert h.fold(0, round_storage=True) == 0
+                assert np.array_equal(nz[i], h.codes), f"refit head {i} codes"
+                assert np.array_equal(bits(nc[i]), bits(h.c)), f"refit head {i} smoothing"
+                assert np.array_equal(bits(nb[i]), bits(h.b)), f"refit head {i} scales"
+        out = codec.window_step_bf16(window, f32_dev(inputs["log_decay"][t]),
+                                     bf16_dev(inputs["beta"][t]), bf16_dev(inputs["keys"][t]),
+                                     bf16_dev(inputs["queries"][t]), bf16_dev(inputs["values"][t]))
+        torch.cuda.synchronize()
+        got = out.view(torch.int16).cpu().numpy().view(np.uint16)
+        pos = next(iter(heads.values())).position.value
+        alpha = window.record_decay[:, pos].cpu().numpy()
+        for i, h in heads.items():
+            token = oracle.qwen_token(alpha[i], inputs["beta"][t][i], inputs["keys"][t][i // 2],
+                                      inputs["queries"][t][i // 2], inputs["values"][t][i])
+            want = h.step(*token, round_storage=True)
+            assert np.array_equal(got[i], oracle.f32_to_bf16_array(want[None])[0]), \
+                f"token {t} head {i}"
+    rows = torch.as_tensor(sample, device=DEV)
+    check_records(codec.WindowStates(window.encoded, None, None,
+                                     window.record_decay[rows], window.record_keys[rows],
+                                     window.record_corrections[rows], window.positions[rows]),
+                  [heads[int(i)] for i in sample], "after 18 tokens")
+
+
 def test_full_window_is_left_untouched_and_reported():
     nheads = 4
     window = _qwen_boundary(nheads, False, seed=3)
@@ -247,11 +302,15 @@ def test_runtime_decode_matches_oracle():
     assert rt.boundary_refits == 1
 
 
-@pytest.mark.parametrize("compensators, iterations", [(False, 0), (True, 0), (True, 8)])
-def test_refit_of_a_partial_window_matches_oracle(compensators, iterations):
-    """A refit at position 7 (the probe case): the folded boundary and the
-    cleared window, bit-identical to the oracle."""
-    case = wc.step_probe_case(states=8, position=7)
+@pytest.mark.parametrize("compensators, iterations, position",
+                         [(False, 0, 7), (True, 0, 7), (True, 8, 7), (False, 0, 0), (True, 0, 0),
+                          (False, 0, 16), (True, 0, 16)])
+def test_refit_of_a_partial_window_matches_oracle(compensators, iterations, position):
+    """A refit at position 7 (the probe case), of an empty window and of a
+    full one: the folded boundary and the cleared window, bit-identical to the
+    oracle.  20 heads, so the quant-only refit's CTAs each take more than one
+    head through the staging pipeline."""
+    case = wc.step_probe_case(states=20, position=position)
     window = window_from_case(case, "provider", compensators)
     heads = wc.window_heads(case, "provider", compensators)
     nxt = codec.window_refit(window, iterations)
