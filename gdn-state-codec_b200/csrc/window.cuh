@@ -324,18 +324,26 @@ inline size_t window_step_smem_bytes() {
 }
 
 // ---------------------------------------------------------------------------
-// Qwen3.5 step with the next head's inputs staged a head ahead.  The same
-// arithmetic as window_step_kernel<true, kComp>; every per-head global read
+// Qwen3.5 steps with the next head's inputs staged a head ahead.  The same
+// arithmetic as window_step_kernel<true, comp>; every per-head global read
 // (codes, records, position, smoothing, scales, compensators and the token's
 // log decay, beta, key, query and value) is a cp.async into one stage that
 // the CTA consumes at the start of the head -- codes into registers, records
 // converted into the chain rows -- and then refills for its next head while
-// this head's suffix, chains and readout run.  Four CTAs per SM (55 KB of
-// shared memory each) for a quant-only boundary, three with compensators.
-// Needs 16-byte aligned key, query and value rows and a 4-byte aligned beta
-// (the host checks and otherwise launches window_step_kernel).
+// this head's suffix, chains and readout run.  Needs 16-byte aligned key,
+// query and value rows and a 4-byte aligned beta (the host checks and
+// otherwise launches window_step_kernel).
+//   window_step_staged_kernel (quant-only boundary): four warps, the
+//     sequential projections on the first lanes before their readout, as in
+//     window_step_kernel; 55 KB of shared memory, four CTAs per SM.
+//   window_step_staged_comp_kernel (rank-4 boundary, whose 41 projections
+//     would spill onto a second warp): a fifth warp runs every projection,
+//     two per lane in one packed add, beside the four readout warps.
 
-struct __align__(16) StepStage {
+// 128-byte aligned: the code rows' swizzle makes a column read conflict-free
+// only when each 128-byte row starts a shared-memory line (measured: 0.49
+// against 0.55-0.59 ms per step when the stage sat 48 or 80 bytes past one).
+struct __align__(128) StepStage {
   uint4 codes[kValues][8];          // provider row v, 16-byte chunk j at j ^ (v & 7)
   uint16_t rkeys[kWindow][kKeys];   // records (binary16)
   uint16_t rcorr[kWindow][kValues];
@@ -352,15 +360,11 @@ struct __align__(16) StepStage {
 };
 
 struct __align__(16) StagedComp {
-  float4 ck[kKeys];                 // compensator keys (fp32) for the chains
   uint2 stage_ck[kKeys];            // staged binary16 compensators
   uint2 stage_cv[kValues];
 };
-struct StagedNoComp {};
 
-// The step's working set (as StepShared, without the compensator keys of a
-// quant-only boundary) and the stage: 55 KB quant-only, four CTAs per SM.
-template <bool kComp>
+// Quant-only step: the working set of window_step_kernel and the stage.
 struct __align__(16) StagedStepShared {
   float suffix[2][kWindow][kRowPad];
   float rkey[kWindow][kRowPad];
@@ -369,14 +373,56 @@ struct __align__(16) StagedStepShared {
   float key[kKeys];
   float query[kKeys];
   float proj[2][kWindow];
+  float rdecay[kWindow];
+  float up;
+  StepStage stage;
+};
+
+// Compensated step.  Chain operand rows: rkey rows 0..15 are the records,
+// row 16 the write key, rows 17..20 the compensator keys by rank; suffix
+// rows 0..15 hold (read, query) decayed by the j newest records, row 16
+// (q, q) for the update chain, row 17 the final pair for the compensator
+// chains.
+constexpr int kStagedCompThreads = kKeys + 32;
+constexpr int kUpdateRow = kWindow;
+constexpr int kCompRow = kWindow + 1;
+constexpr int kFinalRow = kWindow + 1;
+constexpr int kPairRowPad = kKeys + 2;  // f2: 16-byte rows, 8 rows at one key hit 32 banks
+
+struct __align__(16) StagedCompShared {
+  f2 suffix[kWindow + 2][kPairRowPad];
+  float rkey[kWindow + 1 + kRank][kRowPad];
+  float4 sq[kKeys / 2];
+  float c[kKeys];
+  float proj[2][kWindow];
   float cproj[2][kRank];
   float rdecay[kWindow];
   float up;
   StepStage stage;
-  typename std::conditional<kComp, StagedComp, StagedNoComp>::type comp;
+  StagedComp comp;
 };
 
-// This thread's share of head h's stage (all 128 threads issue; one commit).
+// Two sequential dot products at once, sum_k a[k] * (b0[k], b1[k]) for
+// k = 0..127, with a one fp32 row and b a row of pairs (both 16-byte
+// aligned): each key's two products in one packed fma (+0 addend, so that
+// the product is rounded before the add) and one packed add.
+__device__ __forceinline__ f2 chain_dot2(const float* a, const f2* b) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(b);
+  f2 acc = pack2(0.0F, 0.0F);
+#pragma unroll 8
+  for (int k4 = 0; k4 < kKeys / 4; ++k4) {
+    const float4 x = a4[k4];
+    const ulonglong2 y01 = b2[2 * k4], y23 = b2[2 * k4 + 1];
+    acc = add2(acc, mul2_for_add(pack2(x.x, x.x), y01.x));
+    acc = add2(acc, mul2_for_add(pack2(x.y, x.y), y01.y));
+    acc = add2(acc, mul2_for_add(pack2(x.z, x.z), y23.x));
+    acc = add2(acc, mul2_for_add(pack2(x.w, x.w), y23.y));
+  }
+  return acc;
+}
+
+// This thread's share of head h's stage (threads 0..127 issue; one commit).
 template <bool kComp, class Shared>
 __device__ __forceinline__ void step_stage_issue(const StepParams& p, Shared& sh, uint64_t h,
                                                  int t) {
@@ -439,15 +485,13 @@ __device__ __forceinline__ void step_stage_issue(const StepParams& p, Shared& sh
   cp_async_commit();
 }
 
-template <bool kComp>
-__global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
-    window_step_staged_kernel(StepParams p) {
+__global__ void __launch_bounds__(kWinThreads, 4) window_step_staged_kernel(StepParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  StagedStepShared<kComp>& sh = *reinterpret_cast<StagedStepShared<kComp>*>(smem_raw);
+  StagedStepShared& sh = *reinterpret_cast<StagedStepShared*>(smem_raw);
   StepStage& st = sh.stage;
   const int t = threadIdx.x;
   uint64_t head = blockIdx.x;
-  if (head < p.heads) step_stage_issue<kComp>(p, sh, head, t);
+  if (head < p.heads) step_stage_issue<false>(p, sh, head, t);
   for (; head < p.heads; head += gridDim.x) {
     const uint64_t next = head + gridDim.x;
     cp_async_wait<0>();
@@ -457,7 +501,7 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
     if (pos >= kWindow) {  // block-uniform: every thread read the same word
       if (t == 0) report(nullptr, kStatusWindowFull);
       __syncthreads();  // every thread has read the stage
-      if (next < p.heads) step_stage_issue<kComp>(p, sh, next, t);
+      if (next < p.heads) step_stage_issue<false>(p, sh, next, t);
       continue;
     }
     const int np = static_cast<int>(pos);
@@ -476,17 +520,6 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
     sh.query[t] = query_t;
     sh.c[t] = st.c[t];
     const float b_t = st.b[t];
-    float cv_t[kRank] = {0.F, 0.F, 0.F, 0.F};
-    if constexpr (kComp) {
-      const uint2 kw = sh.comp.stage_ck[t];
-      sh.comp.ck[t] = make_float4(half_to_float(kw.x & 0xFFFFu), half_to_float(kw.x >> 16),
-                                  half_to_float(kw.y & 0xFFFFu), half_to_float(kw.y >> 16));
-      const uint2 vw = sh.comp.stage_cv[t];
-      cv_t[0] = half_to_float(vw.x & 0xFFFFu);
-      cv_t[1] = half_to_float(vw.x >> 16);
-      cv_t[2] = half_to_float(vw.y & 0xFFFFu);
-      cv_t[3] = half_to_float(vw.y >> 16);
-    }
     if (t < kWindow) sh.rdecay[t] = st.rdecay[t];
     float rc[kWindow];
 #pragma unroll
@@ -495,7 +528,7 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
       rc[u] = half_to_float(st.rcorr[u][t]);
     }
     __syncthreads();  // the stage is consumed: refill it with the next head
-    if (next < p.heads) step_stage_issue<kComp>(p, sh, next, t);
+    if (next < p.heads) step_stage_issue<false>(p, sh, next, t);
     // ---- suffix-decayed read and query (thread t = key t) -----------------
     {
       float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
@@ -515,24 +548,8 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
     }
     __syncthreads();
     // ---- sequential projections: records, compensators, update -----------
-    const int chains = 2 * np + (kComp ? 2 * kRank : 0) + 1;
-    bool comp_chain = false;
-    if constexpr (kComp) {
-      comp_chain = t >= 2 * np && t < 2 * np + 2 * kRank;
-      if (comp_chain) {
-        const int i = t - 2 * np;
-        const int r = i / kRank, m = i % kRank;
-        const float* ck = reinterpret_cast<const float*>(sh.comp.ck) + m;
-        const float* sq = reinterpret_cast<const float*>(sh.sq) + 2 * r;
-        float acc = 0.0F;
-#pragma unroll 8
-        for (int kk = 0; kk < kKeys; ++kk) {
-          acc = __fadd_rn(acc, __fmul_rn(ck[4 * kk], sq[4 * (kk >> 1) + (kk & 1)]));
-        }
-        sh.cproj[r][m] = acc;
-      }
-    }
-    if (!comp_chain && t < chains) {
+    const int chains = 2 * np + 1;
+    if (t < chains) {
       const float* a = sh.key;
       const float* bq = sh.query;
       float* dst = &sh.up;
@@ -581,13 +598,6 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
     }
     out0 = __fadd_rn(out0, __fmul_rn(div127_any(acc0), b_t));
     out1 = __fadd_rn(out1, __fmul_rn(div127_any(acc1), b_t));
-    if constexpr (kComp) {
-#pragma unroll
-      for (int m = 0; m < kRank; ++m) {
-        out0 = __fadd_rn(out0, __fmul_rn(cv_t[m], sh.cproj[0][m]));
-        out1 = __fadd_rn(out1, __fmul_rn(cv_t[m], sh.cproj[1][m]));
-      }
-    }
     const float correction = __fsub_rn(value_t, out0);
     const float output = __fadd_rn(out1, __fmul_rn(correction, sh.up));
     static_cast<uint16_t*>(p.outputs)[head * kValues + t] =
@@ -605,9 +615,180 @@ __global__ void __launch_bounds__(kWinThreads, kComp ? 3 : 4)
   }
 }
 
+__global__ void __launch_bounds__(kStagedCompThreads, 3)
+    window_step_staged_comp_kernel(StepParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  StagedCompShared& sh = *reinterpret_cast<StagedCompShared*>(smem_raw);
+  StepStage& st = sh.stage;
+  const int t = threadIdx.x;
+  const bool reader = t < kKeys;
+  uint64_t head = blockIdx.x;
+  if (reader && head < p.heads) step_stage_issue<true>(p, sh, head, t);
+  for (; head < p.heads; head += gridDim.x) {
+    const uint64_t next = head + gridDim.x;
+    cp_async_wait<0>();
+    __syncthreads();  // this head's stage has landed; the previous head is done
+    const uint32_t pos = st.position[0];
+    const uint64_t rbase = head * kWindow;
+    if (pos >= kWindow) {  // block-uniform: every thread read the same word
+      if (t == 0) report(nullptr, kStatusWindowFull);
+      __syncthreads();  // every thread has read the stage
+      if (reader && next < p.heads) step_stage_issue<true>(p, sh, next, t);
+      continue;
+    }
+    const int np = static_cast<int>(pos);
+    uint4 zrow[8];
+    float alpha = 0.0F, key_t = 0.0F, read_t = 0.0F, query_t = 0.0F, value_t = 0.0F, b_t = 0.0F;
+    float rc[kWindow];
+    float cv_t[kRank] = {0.F, 0.F, 0.F, 0.F};
+    if (reader) {
+      // ---- consume the stage: codes row t to registers, records, inputs -----
+#pragma unroll
+      for (int j = 0; j < 8; ++j) zrow[j] = st.codes[t][j ^ (t & 7)];
+      alpha = expf(st.log_decay);
+      const float beta = bf16_to_float(static_cast<uint16_t>(st.beta_pair >> (16 * (head & 1))));
+      const float k = bf16_to_float(st.key[t]);
+      key_t = __fmul_rn(beta, k);
+      read_t = __fmul_rn(alpha, k);
+      query_t = __fmul_rn(kQueryScale, bf16_to_float(st.query[t]));
+      value_t = bf16_to_float(st.value[t]);
+      sh.rkey[kUpdateRow][t] = key_t;
+      sh.suffix[kUpdateRow][t] = pack2(query_t, query_t);
+      sh.c[t] = st.c[t];
+      b_t = st.b[t];
+      {
+        const uint2 kw = sh.comp.stage_ck[t];
+        sh.rkey[kCompRow + 0][t] = half_to_float(kw.x & 0xFFFFu);
+        sh.rkey[kCompRow + 1][t] = half_to_float(kw.x >> 16);
+        sh.rkey[kCompRow + 2][t] = half_to_float(kw.y & 0xFFFFu);
+        sh.rkey[kCompRow + 3][t] = half_to_float(kw.y >> 16);
+        const uint2 vw = sh.comp.stage_cv[t];
+        cv_t[0] = half_to_float(vw.x & 0xFFFFu);
+        cv_t[1] = half_to_float(vw.x >> 16);
+        cv_t[2] = half_to_float(vw.y & 0xFFFFu);
+        cv_t[3] = half_to_float(vw.y >> 16);
+      }
+      if (t < kWindow) sh.rdecay[t] = st.rdecay[t];
+#pragma unroll
+      for (int u = 0; u < kWindow; ++u) {
+        sh.rkey[u][t] = half_to_float(st.rkeys[u][t]);
+        rc[u] = half_to_float(st.rcorr[u][t]);
+      }
+    }
+    __syncthreads();  // the stage is consumed: refill it with the next head
+    if (reader) {
+      if (next < p.heads) step_stage_issue<true>(p, sh, next, t);
+      // ---- suffix-decayed read and query (thread t = key t) ---------------
+      float s0 = read_t, s1 = __fmul_rn(alpha, query_t);
+#pragma unroll
+      for (int u = kWindow - 1; u >= 0; --u) {  // record u is read with suffix np-1-u
+        if (u < np) {
+          sh.suffix[np - 1 - u][t] = pack2(s0, s1);
+          const float d = sh.rdecay[u];
+          s0 = __fmul_rn(s0, d);
+          s1 = __fmul_rn(s1, d);
+        }
+      }
+      float* sq = reinterpret_cast<float*>(sh.sq) + 4 * (t >> 1) + (t & 1);
+      sq[0] = s0;
+      sq[2] = s1;
+      sh.suffix[kFinalRow][t] = pack2(s0, s1);
+    }
+    __syncthreads();
+    float acc0 = 0.0F, acc1 = 0.0F;
+    if (!reader) {
+      // ---- chain warp: two sequential projections per lane -----------------
+      // lane u < np: record u against both reads (suffix row np-1-u); lane
+      // np: the write key against the query; lanes np+1..np+4 (with
+      // compensators): compensator key m against the final suffix pair.
+      const int lane = t - kKeys;
+      const int chains = np + 1 + kRank;
+      if (lane < chains) {
+        int arow = kUpdateRow, brow = kUpdateRow;
+        float* dst0 = &sh.up;
+        float* dst1 = nullptr;
+        if (lane < np) {
+          arow = lane;
+          brow = np - 1 - lane;
+          dst0 = &sh.proj[0][lane];
+          dst1 = &sh.proj[1][lane];
+        } else if (lane > np) {
+          const int m = lane - np - 1;
+          arow = kCompRow + m;
+          brow = kFinalRow;
+          dst0 = &sh.cproj[0][m];
+          dst1 = &sh.cproj[1][m];
+        }
+        const f2 acc = chain_dot2(&sh.rkey[arow][0], &sh.suffix[brow][0]);
+        *dst0 = lo2(acc);
+        if (dst1 != nullptr) *dst1 = hi2(acc);
+      }
+    } else {
+      // ---- boundary readout of column t for both reads --------------------
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t words[4] = {zrow[i].x, zrow[i].y, zrow[i].z, zrow[i].w};
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int k0 = 16 * i + 4 * w;
+          f2 z01, z23;
+          unpack_codes(words[w], z01, z23);
+          const float4 c4 = *reinterpret_cast<const float4*>(&sh.c[k0]);
+          const f2 zc01 = mul2(z01, pack2(c4.x, c4.y));
+          const f2 zc23 = mul2(z23, pack2(c4.z, c4.w));
+          const float4 sa = sh.sq[k0 >> 1], sb = sh.sq[(k0 >> 1) + 1];
+          f2 p0 = mul2_for_add(zc01, pack2(sa.x, sa.y));
+          f2 p1 = mul2_for_add(zc01, pack2(sa.z, sa.w));
+          acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+          acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
+          p0 = mul2_for_add(zc23, pack2(sb.x, sb.y));
+          p1 = mul2_for_add(zc23, pack2(sb.z, sb.w));
+          acc0 = __fadd_rn(__fadd_rn(acc0, lo2(p0)), hi2(p0));
+          acc1 = __fadd_rn(__fadd_rn(acc1, lo2(p1)), hi2(p1));
+        }
+      }
+    }
+    __syncthreads();
+    if (reader) {
+      // ---- column t: records newest first, boundary, compensators ---------
+      float out0 = 0.0F, out1 = 0.0F;
+#pragma unroll
+      for (int u = kWindow - 1; u >= 0; --u) {
+        if (u < np) {
+          out0 = __fadd_rn(out0, __fmul_rn(rc[u], sh.proj[0][u]));
+          out1 = __fadd_rn(out1, __fmul_rn(rc[u], sh.proj[1][u]));
+        }
+      }
+      out0 = __fadd_rn(out0, __fmul_rn(div127_any(acc0), b_t));
+      out1 = __fadd_rn(out1, __fmul_rn(div127_any(acc1), b_t));
+      {
+#pragma unroll
+        for (int m = 0; m < kRank; ++m) {
+          out0 = __fadd_rn(out0, __fmul_rn(cv_t[m], sh.cproj[0][m]));
+          out1 = __fadd_rn(out1, __fmul_rn(cv_t[m], sh.cproj[1][m]));
+        }
+      }
+      const float correction = __fsub_rn(value_t, out0);
+      const float output = __fadd_rn(out1, __fmul_rn(correction, sh.up));
+      static_cast<uint16_t*>(p.outputs)[head * kValues + t] =
+          __bfloat16_as_ushort(__float2bfloat16_rn(output));
+      if (!isfinite(output)) report(nullptr, kStatusWindowNonFinite);
+      // ---- append the record -------------------------------------------------
+      p.w.record_keys[(rbase + np) * kKeys + t] = float_to_half_bits(key_t);
+      p.w.record_corrections[(rbase + np) * kValues + t] = float_to_half_bits(correction);
+      if (t == 0) {
+        p.w.record_decay[rbase + np] = alpha;
+        p.w.positions[head * kPositionStride] = pos + 1u;
+      }
+    }
+    // The barrier at the top of the next head orders these shared-memory
+    // reads before the next head's writes.
+  }
+}
+
 template <bool kComp>
 inline size_t window_step_staged_smem_bytes() {
-  return sizeof(StagedStepShared<kComp>);
+  return kComp ? sizeof(StagedCompShared) : sizeof(StagedStepShared);
 }
 
 // ---------------------------------------------------------------------------
@@ -1157,12 +1338,13 @@ inline cudaError_t prepare_step_variant(int* blocks) {
 
 template <bool kComp>
 inline cudaError_t prepare_staged_variant(int* blocks) {
-  const auto kernel = window_step_staged_kernel<kComp>;
+  const auto kernel = kComp ? window_step_staged_comp_kernel : window_step_staged_kernel;
+  const int threads = kComp ? kStagedCompThreads : kWinThreads;
   const size_t smem = window_step_staged_smem_bytes<kComp>();
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, kWinThreads, smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kernel, threads, smem);
 }
 
 inline cudaError_t prepare_window(WindowBlocks* b) {
@@ -1203,14 +1385,15 @@ inline cudaError_t launch_window_step_staged(bool comp, const StepParams& p, int
                                              cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kWinThreads);
   cfg.stream = stream;
   if (comp) {
+    cfg.blockDim = dim3(kStagedCompThreads);
     cfg.dynamicSmemBytes = window_step_staged_smem_bytes<true>();
-    return cudaLaunchKernelEx(&cfg, window_step_staged_kernel<true>, p);
+    return cudaLaunchKernelEx(&cfg, window_step_staged_comp_kernel, p);
   }
+  cfg.blockDim = dim3(kWinThreads);
   cfg.dynamicSmemBytes = window_step_staged_smem_bytes<false>();
-  return cudaLaunchKernelEx(&cfg, window_step_staged_kernel<false>, p);
+  return cudaLaunchKernelEx(&cfg, window_step_staged_kernel, p);
 }
 
 inline cudaError_t launch_window_step(bool qwen, bool comp, const StepParams& p, int grid,
