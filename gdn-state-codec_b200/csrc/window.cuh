@@ -365,7 +365,7 @@ struct __align__(16) StagedComp {
 };
 
 // Quant-only step: the working set of window_step_kernel and the stage.
-struct __align__(16) StagedStepShared {
+struct __align__(128) StagedStepShared {
   float suffix[2][kWindow][kRowPad];
   float rkey[kWindow][kRowPad];
   float4 sq[kKeys / 2];
@@ -389,7 +389,7 @@ constexpr int kCompRow = kWindow + 1;
 constexpr int kFinalRow = kWindow + 1;
 constexpr int kPairRowPad = kKeys + 2;  // f2: 16-byte rows, 8 rows at one key hit 32 banks
 
-struct __align__(16) StagedCompShared {
+struct __align__(128) StagedCompShared {
   f2 suffix[kWindow + 2][kPairRowPad];
   float rkey[kWindow + 1 + kRank][kRowPad];
   float4 sq[kKeys / 2];
