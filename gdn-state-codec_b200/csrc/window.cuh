@@ -92,9 +92,11 @@ struct __align__(16) StepShared {
   float up;                             // key . query
 };
 
-struct __align__(16) StepSharedCapsule {
+struct __align__(128) StepSharedCapsule {
   StepShared s;
-  int8_t codes[kElements];  // capsule-layout codes staged for column reads
+  // Capsule-layout codes staged for column reads; 128-byte aligned so that a
+  // warp's 32-byte piece of a 128-byte key row never straddles two lines.
+  alignas(128) int8_t codes[kElements];
 };
 
 __device__ __forceinline__ float half_to_float(uint16_t h) {
