@@ -136,36 +136,44 @@ __device__ __forceinline__ float div127_any(float a) {
 }
 
 // --------------------------------------------------------------------------
-// Correctly rounded quotients a / c for many a and one divisor c, from
-// y = RN(1/c) and nc = -c, with two fused-multiply-add corrections:
-//   q0 = RN(a * y)           within 1.5 ulp of a / c
-//   q1 = q0 + (a - q0 c) y   within 0.5 ulp + 2^-46 relative: faithful
-//   q2 = q1 + (a - q1 c) y   = RN(a / c)
-// The remainder a - q1 c of a faithful quotient is exactly representable and
-// the final fma then rounds correctly when y = RN(1/c) (Markstein, "Computation
-// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
-// Dev. 34(1), 1990; Muller et al., "Handbook of Floating-Point Arithmetic",
-// 2nd ed., 2018, sec. 4.7 and 5.3).  Preconditions: c and 1/c normal,
-// |a| >= 2^-102 (no remainder underflows) and a / c normal, or a == 0.
-// Callers check the ranges per row / column and fall back to IEEE division
-// outside them; tests/test_gpu_division.py compares the routine with IEEE
-// division on the device.
-__device__ __forceinline__ f2 div2_exact(f2 a, f2 y, f2 nc) {
-  const f2 q0 = mul2(a, y);
-  const f2 r0 = fma2(q0, nc, a);
-  const f2 q1 = fma2(r0, y, q0);
-  const f2 r1 = fma2(q1, nc, a);
-  return fma2(r1, y, q1);
+// Correctly rounded quotients a / c for many a and one divisor c, from a
+// two-term reciprocal y = RN(1/c), yl = RN((1 - c y) y) and nc = -c, with one
+// fused-multiply-add correction:
+//   q0 = RN(a y + RN(a yl))   faithful (within 1 ulp of a / c)
+//   q  = RN(q0 + (a - q0 c) y) = RN(a / c)
+// y + yl equals 1/c within about 2^-47 relative: 1 - c y is exact (the
+// remainder of the faithful reciprocal y), and (1 - c y) y = (1/c - y)(c y)
+// with |1 - c y| <= 2^-24.  So a y + RN(a yl) lies within 2^-46 |a / c| of
+// a / c and its one rounding stays below one ulp.  The remainder a - q0 c of
+// a faithful quotient is exactly representable and the last fma then rounds
+// correctly because y = RN(1/c) (Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
+// 1990; Muller et al., "Handbook of Floating-Point Arithmetic", 2nd ed.,
+// 2018, sec. 4.7 and 5.3).  Four operations where RN(a y) and two
+// corrections take five.  Preconditions: c and 1/c normal, |a| >= 2^-102 (no
+// remainder underflows) and |a / c| >= 2^-125, or a == 0.  Callers check
+// the ranges per row / column and fall back to IEEE division outside them;
+// tests/test_gpu_division.py compares the routine with IEEE division on the
+// device.
+__device__ __forceinline__ float recip_lo(float c, float y) {
+  return __fmul_rn(__fmaf_rn(-c, y, 1.0F), y);
 }
-__device__ __forceinline__ float4 div4_exact(float4 a, float4 y, float4 nc) {
-  const f2 lo = div2_exact(pack2(a.x, a.y), pack2(y.x, y.y), pack2(nc.x, nc.y));
-  const f2 hi = div2_exact(pack2(a.z, a.w), pack2(y.z, y.w), pack2(nc.z, nc.w));
+__device__ __forceinline__ f2 div2_exact(f2 a, f2 y, f2 yl, f2 nc) {
+  const f2 q0 = fma2(a, y, mul2(a, yl));
+  const f2 r = fma2(q0, nc, a);
+  return fma2(r, y, q0);
+}
+__device__ __forceinline__ float4 div4_exact(float4 a, float4 y, float4 yl, float4 nc) {
+  const f2 lo = div2_exact(pack2(a.x, a.y), pack2(y.x, y.y), pack2(yl.x, yl.y),
+                           pack2(nc.x, nc.y));
+  const f2 hi = div2_exact(pack2(a.z, a.w), pack2(y.z, y.w), pack2(yl.z, yl.w),
+                           pack2(nc.z, nc.w));
   return make_float4(lo2(lo), hi2(lo), lo2(hi), hi2(hi));
 }
-__device__ __forceinline__ float4 div4_exact_s(float4 a, float y, float nc) {
-  const f2 yy = pack2(y, y), cc = pack2(nc, nc);
-  const f2 lo = div2_exact(pack2(a.x, a.y), yy, cc);
-  const f2 hi = div2_exact(pack2(a.z, a.w), yy, cc);
+__device__ __forceinline__ float4 div4_exact_s(float4 a, float y, float yl, float nc) {
+  const f2 yy = pack2(y, y), ll = pack2(yl, yl), cc = pack2(nc, nc);
+  const f2 lo = div2_exact(pack2(a.x, a.y), yy, ll, cc);
+  const f2 hi = div2_exact(pack2(a.z, a.w), yy, ll, cc);
   return make_float4(lo2(lo), hi2(lo), lo2(hi), hi2(hi));
 }
 

@@ -25,7 +25,8 @@ __global__ void division_selftest_kernel(const float* a, const float* c, float* 
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
     const float ci = c[i];
-    out[i] = div4_exact_s(make_float4(a[i], 0.F, 0.F, 0.F), __frcp_rn(ci), -ci).x;
+    const float y = __frcp_rn(ci);
+    out[i] = div4_exact_s(make_float4(a[i], 0.F, 0.F, 0.F), y, recip_lo(ci, y), -ci).x;
   }
 }
 

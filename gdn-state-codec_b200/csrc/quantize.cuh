@@ -20,10 +20,11 @@
 //  * the smoothing sums run in double (tree order, with a proof-backed check
 //    that sends the rare order-sensitive rows to the reference's sequential
 //    order); every smoothed value s = R / c is computed correctly rounded from
-//    RN(1/c) by two packed fma corrections (div4_exact), so the per-value
-//    maxima b are exact without any search; codes come from one multiply by
-//    RN(127 / b), and the few elements within the proven error band of a
-//    rounding boundary take the exact code by IEEE division (out of line).
+//    the two-term reciprocal of c by one packed fma correction (div4_exact),
+//    so the per-value maxima b are exact without any search; codes come from
+//    one fma of s and RN(127 / b) with the rounding constant, and the few
+//    elements within the proven error band of a rounding boundary take the
+//    exact code by IEEE division (out of line).
 //  * thread tiles (64 elements per thread) keep the double-precision
 //    reduction mostly inside a thread: capsule layout (row sums over values)
 //    uses 4 rows x 16 columns, provider layout (column sums over values)
@@ -39,13 +40,17 @@ constexpr int kQBlocksPerSm = 2;                    // independent head streams 
 constexpr int kGroupWarps = kQThreads / 32;         // 8
 constexpr int kWarpRows = kKeys / kGroupWarps;      // 16 rows of a head per warp
 
-// Codes: with km = RN(127 / b) = (127 / b)(1 + e1), the approximation
-// t' = RN(s * km) = T (1 + e1)(1 + e2) and the reference's
-// t = RN(RN(s / b) * 127) = T (1 + e3)(1 + e4) of T = 127 s / b, |T| <= 127,
-// |e_i| <= 2^-24, differ by at most 127 * 2^-22 * (1 + 2^-24) < 2^-15.  A code
-// is therefore decided from t' unless t' lies within 2^-15 of a rounding
-// boundary n + 0.5 (ties of t included); those elements take the exact code.
-constexpr float kAmbiguous = 0.5F - 0x1p-15F;
+// Codes: with km = RN(127 / b) = (127 / b)(1 + e1), the exact product
+// s * km = T (1 + e1) and the reference's t = RN(RN(s / b) * 127) =
+// T (1 + e3)(1 + e4) of T = 127 s / b, |T| <= 127, |e_i| <= u = 2^-24, differ
+// by at most 127 (3u + u^2) < 381.01 u.  One fma forms u' = RN(s km + M) with
+// M = 1.5 * 2^23, i.e. M + n for the integer n nearest to s km (the low byte
+// of u' is n as int8), and a second gives d = RN(s km - n) within u / 4 of
+// s km - n (M - u' = -n is exact).  If |d| <= 0.5 - 384 u, then
+// |t - n| <= 0.5 - 384 u + u / 4 + 381.01 u < 0.5 and the reference's lround
+// gives n as well; every other element (ties of t included) takes the exact
+// code.  tests/division_check.c checks the rule on the CPU.
+constexpr float kAmbiguous = 0.5F - 0x1.8p-16F;  // 0.5 - 384 * 2^-24
 // Fast-path ranges: a per-value maximum b in [2^-64, 2^100] and smoothing in
 // [2^-14, 2^100] keep every element that can be a maximum or have a nonzero
 // code (|s| >= b / 254) inside div4_exact's preconditions (|R| >= 2^-102,
@@ -87,6 +92,7 @@ struct __align__(128) QuantizeGroupShared {
   };
   float key_c[kKeys];                  // smoothing per key
   float key_y[kKeys];                  // RN(1/c) per key
+  float key_yl[kKeys];                 // RN((1 - c y) y): second reciprocal term
   float val_b[kValues];                // exact per-value maximum
   float val_km[kValues];               // RN(127 / b), 0 on the IEEE path
   uint32_t val_exact[kValues];         // IEEE path: maximum (bits)
@@ -135,13 +141,13 @@ __device__ __forceinline__ bool fast_smoothing(float c) {
 // the magic constant; returns the packed int8x4 word and reports whether any
 // element lies within the ambiguity band of a rounding boundary.
 __device__ __forceinline__ uint32_t approx_codes(float4 s, float4 km, bool* amb) {
-  const f2 t01 = mul2(pack2(s.x, s.y), pack2(km.x, km.y));
-  const f2 t23 = mul2(pack2(s.z, s.w), pack2(km.z, km.w));
+  const f2 s01 = pack2(s.x, s.y), s23 = pack2(s.z, s.w);
+  const f2 k01 = pack2(km.x, km.y), k23 = pack2(km.z, km.w);
   const f2 magic = pack2(kRoundMagic, kRoundMagic);
-  const f2 u01 = add2(t01, magic);
-  const f2 u23 = add2(t23, magic);
-  const f2 d01 = sub2(t01, sub2(u01, magic));
-  const f2 d23 = sub2(t23, sub2(u23, magic));
+  const f2 u01 = fma2(s01, k01, magic);
+  const f2 u23 = fma2(s23, k23, magic);
+  const f2 d01 = fma2(s01, k01, sub2(magic, u01));
+  const f2 d23 = fma2(s23, k23, sub2(magic, u23));
   const float worst = fmaxf(fmaxf(fabsf(lo2(d01)), fabsf(hi2(d01))),
                             fmaxf(fabsf(lo2(d23)), fabsf(hi2(d23))));
   *amb = !(worst <= kAmbiguous);
@@ -151,9 +157,8 @@ __device__ __forceinline__ uint32_t approx_codes(float4 s, float4 km, bool* amb)
 }
 
 __device__ __forceinline__ bool approx_ambiguous(float s, float km) {
-  const float t = __fmul_rn(s, km);
-  const float u = __fadd_rn(t, kRoundMagic);
-  const float d = __fsub_rn(t, __fsub_rn(u, kRoundMagic));
+  const float u = __fmaf_rn(s, km, kRoundMagic);
+  const float d = __fmaf_rn(s, km, __fsub_rn(kRoundMagic, u));
   return !(fabsf(d) <= kAmbiguous);
 }
 
@@ -350,7 +355,9 @@ __device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p,
     if (lane < kWarpRows) {
       const float c = __ldg(p.smoothing_in + head * kKeys + row_base + lane);
       gs.key_c[row_base + lane] = c;
-      gs.key_y[row_base + lane] = __frcp_rn(c);
+      const float y = __frcp_rn(c);
+      gs.key_y[row_base + lane] = y;
+      gs.key_yl[row_base + lane] = recip_lo(c, y);
     }
   } else {
     double part[4];
@@ -388,7 +395,9 @@ __device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p,
     if ((lane & 1) == 0) {
       const int r = row_base + 4 * my_j + g;
       gs.key_c[r] = c;
-      gs.key_y[r] = __frcp_rn(c);
+      const float y = __frcp_rn(c);
+      gs.key_y[r] = y;
+      gs.key_yl[r] = recip_lo(c, y);
       p.smoothing[head * kKeys + r] = c;
     }
   }
@@ -400,9 +409,10 @@ __device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p,
   for (int j = 0; j < 4; ++j) {
     const int r = row_base + 4 * j + g;
     const float y = gs.key_y[r];
+    const float yl = gs.key_yl[r];
     const float nc = -gs.key_c[r];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) t.v[j][c] = div4_exact_s(t.v[j][c], y, nc);
+    for (int c = 0; c < 4; ++c) t.v[j][c] = div4_exact_s(t.v[j][c], y, yl, nc);
   }
   float4 pm[4];
 #pragma unroll
@@ -523,7 +533,9 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
       if (!flag) p.smoothing[head * kKeys + gtid] = c;
     }
     gs.key_c[gtid] = c;
-    gs.key_y[gtid] = __frcp_rn(c);
+    const float y = __frcp_rn(c);
+    gs.key_y[gtid] = y;
+    gs.key_yl[gtid] = recip_lo(c, y);
     gs.col_flag[gtid] = flag;
   }
   // B2: smoothing ready.  With computed smoothing it also tells whether a
@@ -542,7 +554,9 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
         for (int r = 0; r < kValues; ++r) seq += fabsf(gs.colbuf[r]);
         const float c = smoothing_from_sum(seq);
         gs.key_c[k] = c;
-        gs.key_y[k] = __frcp_rn(c);
+        const float y = __frcp_rn(c);
+        gs.key_y[k] = y;
+        gs.key_yl[k] = recip_lo(c, y);
         p.smoothing[head * kKeys + k] = c;
       }
       group_sync(group);
@@ -553,11 +567,12 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
   // -- exact smoothed values and row maxima (warp-local) ------------------------------
   const float4 c4 = reinterpret_cast<const float4*>(gs.key_c)[lane];
   const float4 y4 = reinterpret_cast<const float4*>(gs.key_y)[lane];
+  const float4 yl4 = reinterpret_cast<const float4*>(gs.key_yl)[lane];
   const float4 nc4 = make_float4(-c4.x, -c4.y, -c4.z, -c4.w);
   float rm[kWarpRows];
 #pragma unroll
   for (int j = 0; j < kWarpRows; ++j) {
-    v[j] = div4_exact(v[j], y4, nc4);
+    v[j] = div4_exact(v[j], y4, yl4, nc4);
     rm[j] = absmax4(v[j]);
   }
   {

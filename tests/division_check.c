@@ -13,13 +13,22 @@
  *       with |a| >= 2^-112 (both signs), zero, the infinities and NaN.
  *
  *   markstein <threads> <samples per thread>
- *       a / c from y = RN(1/c): q0 = RN(a*y), then twice r = fma(-q, c, a),
- *       q = fma(r, y, q) (Markstein, "Computation of elementary functions on
- *       the IBM RISC System/6000 processor", IBM J. R&D 34(1), 1990).
- *       Checked on random operands over the kernels' fast-path ranges
- *       (c in [2^-14, 2^100], |a| >= 2^-102, normal quotient) and on
- *       operands built so that a / c lies within a few ulps of a rounding
+ *       a / c from the two-term reciprocal y = RN(1/c), yl = RN((1 - c y) y):
+ *       the faithful q0 = fma(a, y, RN(a yl)), then one correction
+ *       r = fma(-q0, c, a), q = fma(r, y, q0) (Markstein, "Computation of
+ *       elementary functions on the IBM RISC System/6000 processor", IBM
+ *       J. R&D 34(1), 1990).  Checked on random operands over the kernels'
+ *       fast-path ranges (c in [2^-14, 2^100], |a| >= 2^-102, quotient of
+ *       magnitude >= 2^-125), on quotients at the bottom of that range, and
+ *       on operands built so that a / c lies within a few ulps of a rounding
  *       midpoint -- the hard cases of correctly rounded division.
+ *
+ *   codes <threads> <samples per thread>
+ *       the quantizer's code rule from one fma, u = fma(s, RN(127 / b), M)
+ *       with M = 1.5 * 2^23, and its flag |fma(s, km, M - u)| > 0.5 - 3 * 2^-17:
+ *       every unflagged code equals the reference's
+ *       clamp(lround(RN(RN(s / b) * 127))), on random values and on values
+ *       next to rounding boundaries.
  *
  * Prints one line "<mode> checked=<n> mismatches=<m>" and exits 0 when m is 0.
  * Compiled with -ffp-contract=off so that every operation rounds as written;
@@ -114,12 +123,11 @@ static int run_div127(int threads) {
 
 static float div_markstein(float a, float c) {
   const float y = 1.0F / c;  /* RN(1/c), as __frcp_rn on the device */
+  const float yl = fmaf(-c, y, 1.0F) * y;  /* second reciprocal term */
   const float nc = -c;
-  const float q0 = a * y;
-  const float r0 = fmaf(q0, nc, a);
-  const float q1 = fmaf(r0, y, q0);
-  const float r1 = fmaf(q1, nc, a);
-  return fmaf(r1, y, q1);
+  const float q0 = fmaf(a, y, a * yl);  /* faithful */
+  const float r = fmaf(q0, nc, a);
+  return fmaf(r, y, q0);
 }
 
 static uint64_t next(uint64_t* s) { /* SplitMix64 */
@@ -146,7 +154,7 @@ struct Sample {
 static int in_range(float a, float c) {
   const float q = a / c;
   return fabsf(a) >= 0x1p-102F && fabsf(c) >= 0x1p-14F && fabsf(c) <= 0x1p100F &&
-         isnormal(q) && isfinite(a);
+         isfinite(q) && fabsf(q) >= 0x1p-125F && isfinite(a);
 }
 
 static void check(struct Sample* s, float a, float c) {
@@ -181,6 +189,12 @@ static void* markstein_worker(void* arg) {
     /* (3) exact quotients: a = q * c when representable */
     const float a3 = q * c;
     if ((double)a3 == (double)q * (double)c) check(s, a3, c);
+    /* (4) quotients at the bottom of the range, where RN(a yl) is tiny */
+    const float cl = fabsf(random_float(&state, 60, 99));
+    const float ql = random_float(&state, -125, -110);
+    const float a4 = (float)((double)ql * (double)cl);
+    check(s, a4, cl);
+    check(s, nextafterf(a4, INFINITY), cl);
   }
   return NULL;
 }
@@ -213,11 +227,105 @@ static int run_markstein(int threads, uint64_t samples) {
   return bad == 0 ? 0 : 1;
 }
 
+/* ---- codes from one fma ----------------------------------------------------- */
+
+/* The quantizer's code rule: km = RN(127 / b), u = fma(s, km, M) with
+ * M = 1.5 * 2^23, d = fma(s, km, M - u).  When |d| <= 0.5 - 3 * 2^-17 the code is
+ * u - M; otherwise the element is flagged for the exact path.  An unflagged
+ * code must equal the reference's clamp(lround(RN(RN(s / b) * 127))). */
+struct CodeSample {
+  uint64_t seed, samples, checked, flagged, mismatches, random_flagged;
+  float bad_s, bad_b;
+};
+
+static int check_code(struct CodeSample* cs, float s, float b) {
+  if (!(fabsf(s) <= b)) return 0;
+  const float km = 127.0F / b;
+  const float magic = 12582912.0F;
+  const float u = fmaf(s, km, magic);
+  const float d = fmaf(s, km, magic - u);
+  ++cs->checked;
+  if (!(fabsf(d) <= 0.5F - 0x1.8p-16F)) {
+    ++cs->flagged;
+    return 1;
+  }
+  long want = lroundf((s / b) * 127.0F);
+  want = want < -127 ? -127 : (want > 127 ? 127 : want);
+  if ((long)(u - magic) != want) {
+    if (cs->mismatches == 0) {
+      cs->bad_s = s;
+      cs->bad_b = b;
+    }
+    ++cs->mismatches;
+  }
+  return 0;
+}
+
+static void* code_worker(void* arg) {
+  struct CodeSample* cs = (struct CodeSample*)arg;
+  uint64_t state = cs->seed;
+  for (uint64_t i = 0; i < cs->samples; ++i) {
+    const float b = fabsf(random_float(&state, -64, 99));
+    /* (1) a random smoothed value in [-b, b] */
+    const uint64_t r = next(&state);
+    const float s = (float)(((double)(r >> 11) * 0x1p-53 * 2.0 - 1.0) * (double)b);
+    cs->random_flagged += (uint64_t)check_code(cs, s, b);
+    /* (2) values whose scaled code lies next to a rounding boundary n + 1/2 */
+    const long n = (long)(next(&state) % 254u) - 127;
+    const float t = (float)((double)n + 0.5);
+    const float s2 = (float)((double)t * (double)b / 127.0);
+    float v = s2;
+    for (int k = 0; k < 4; ++k) v = nextafterf(v, -INFINITY);
+    for (int k = 0; k < 9; ++k, v = nextafterf(v, INFINITY)) check_code(cs, v, b);
+    /* (3) the maximum itself and its neighbours */
+    check_code(cs, b, b);
+    check_code(cs, -b, b);
+    check_code(cs, nextafterf(b, 0.0F), b);
+  }
+  return NULL;
+}
+
+static int run_codes(int threads, uint64_t samples) {
+  struct CodeSample* cs = calloc((size_t)threads, sizeof *cs);
+  pthread_t* tid = calloc((size_t)threads, sizeof *tid);
+  for (int t = 0; t < threads; ++t) {
+    cs[t].seed = 0xC0DEull + 104729ull * (uint64_t)t;
+    cs[t].samples = samples;
+    pthread_create(&tid[t], NULL, code_worker, &cs[t]);
+  }
+  uint64_t checked = 0, flagged = 0, bad = 0, random_flagged = 0;
+  float bad_s = 0.0F, bad_b = 0.0F;
+  for (int t = 0; t < threads; ++t) {
+    pthread_join(tid[t], NULL);
+    checked += cs[t].checked;
+    flagged += cs[t].flagged;
+    random_flagged += cs[t].random_flagged;
+    if (cs[t].mismatches && !bad) {
+      bad_s = cs[t].bad_s;
+      bad_b = cs[t].bad_b;
+    }
+    bad += cs[t].mismatches;
+  }
+  printf("codes checked=%llu flagged=%llu random=%llu random_flagged=%llu mismatches=%llu",
+         (unsigned long long)checked, (unsigned long long)flagged,
+         (unsigned long long)samples * (uint64_t)threads, (unsigned long long)random_flagged,
+         (unsigned long long)bad);
+  if (bad) printf(" first=%a/%a", (double)bad_s, (double)bad_b);
+  printf("\n");
+  free(cs);
+  free(tid);
+  return bad == 0 ? 0 : 1;
+}
+
 int main(int argc, char** argv) {
   if (argc >= 3 && strcmp(argv[1], "div127") == 0) return run_div127(atoi(argv[2]));
   if (argc >= 4 && strcmp(argv[1], "markstein") == 0) {
     return run_markstein(atoi(argv[2]), strtoull(argv[3], NULL, 10));
   }
-  fprintf(stderr, "usage: %s div127 <threads> | markstein <threads> <samples>\n", argv[0]);
+  if (argc >= 4 && strcmp(argv[1], "codes") == 0) {
+    return run_codes(atoi(argv[2]), strtoull(argv[3], NULL, 10));
+  }
+  fprintf(stderr, "usage: %s div127 <threads> | markstein|codes <threads> <samples>\n",
+          argv[0]);
   return 2;
 }

@@ -4,9 +4,10 @@ The quantizer and the projection replace IEEE division by faster sequences
 that must round exactly like IEEE division for the codes to stay bit-exact:
   * a / 127 as fma(a, zh, RN(a * zl)) -- checked for every float with
     |a| >= 2^-112 (the kernels send smaller |a| to IEEE division);
-  * a / c from RN(1/c) with two fma corrections -- checked on hundreds of
-    millions of operands over the kernels' fast-path ranges, including
-    quotients next to rounding midpoints.
+  * a / c from the two-term reciprocal RN(1/c), RN((1 - c RN(1/c)) RN(1/c))
+    with one fma correction -- checked on hundreds of millions of operands
+    over the kernels' fast-path ranges, including quotients next to rounding
+    midpoints and at the bottom of the range.
 tests/division_check.c holds the restatements; the device versions are
 compared with IEEE division on the GPU by test_gpu_division.py.
 """
@@ -50,3 +51,12 @@ def test_markstein_quotients(checker):
     fields = dict(item.split("=") for item in line.split()[1:])
     assert int(fields["mismatches"]) == 0, line
     assert int(fields["checked"]) > 10_000_000
+
+
+def test_code_rule(checker):
+    line = _run(checker, "codes", str(THREADS), str(2_000_000))
+    fields = dict(item.split("=") for item in line.split()[1:])
+    assert int(fields["mismatches"]) == 0, line
+    assert int(fields["checked"]) > 10_000_000
+    # the flag band is narrow: random values are flagged about 2^-13 of the time
+    assert int(fields["random_flagged"]) < int(fields["random"]) // 1000

@@ -1,6 +1,7 @@
-"""The quantizer's exact division (RN(1/c) and two fma corrections, used for
-every smoothed value s = R / c) against IEEE float32 division, on the device,
-over random and adversarial operands inside the routine's documented range."""
+"""The quantizer's exact division (the two-term reciprocal of c and one fma
+correction, used for every smoothed value s = R / c) against IEEE float32
+division, on the device, over random and adversarial operands inside the
+routine's documented range."""
 
 from __future__ import annotations
 
