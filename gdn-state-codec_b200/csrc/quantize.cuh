@@ -13,8 +13,8 @@
 // Design (HBM-bound: 64 KiB read + 17 KiB written per head):
 //  * persistent 256-thread CTAs, two per SM.  Each walks its own sequence of
 //    heads with one 64 KiB shared-memory landing buffer filled by a single TMA
-//    bulk copy (cp.async.bulk + mbarrier); as soon as the CTA holds a head in
-//    registers the buffer takes its next head.  The two CTAs of an SM drift
+//    bulk copy (cp.async.bulk + mbarrier, normal L2 policy); as soon as the
+//    CTA holds a head in registers the buffer takes its next head.  The two CTAs of an SM drift
 //    out of phase, so one's barriers and reductions overlap the other's
 //    arithmetic, and two heads are in flight per SM.
 //  * the smoothing sums run in double (tree order, with a proof-backed check
@@ -179,13 +179,18 @@ __device__ __forceinline__ uint64_t next_item(const QuantizeParams& p, uint64_t 
   return item;
 }
 
+// The head's copy keeps the normal L2 policy, not evict-first: the rare
+// exact-code and re-sum paths re-read a few rows of the head from global
+// memory right after the head is consumed, and with evict-first those reads
+// went to DRAM (0.850 -> 0.81-0.84 ms capsule, 0.900 -> 0.861 ms provider at
+// 61,440 heads, same outputs).
 __device__ __forceinline__ void issue_head(const QuantizeParams& p, QuantizeGroupShared& gs,
                                            int64_t head) {
   fence_proxy_async();
   if (p.arm_only != 0u) return;  // test support: only the first head is armed
   mbar_expect_tx(&gs.full, kElements * sizeof(float));
   bulk_load(gs.stage, p.state + static_cast<uint64_t>(head) * kElements, kElements * sizeof(float),
-            &gs.full, evict_first_policy());
+            &gs.full, evict_normal_policy());
 }
 
 __device__ __forceinline__ float state_at(const QuantizeParams& p, int64_t head, int row, int col) {
