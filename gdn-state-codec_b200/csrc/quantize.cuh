@@ -633,10 +633,10 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
 // near a rounding boundary records (head, mask) and writes the exact codes
 // after the launch's last head, so the IEEE divisions and the re-read of the
 // rows no longer hold its warp back from the next head's block barriers
-// (0.812 -> 0.763 ms at 61,440 capsule heads, 0.863 -> 0.816 ms provider).  The late pass uses global
-// memory only: the input rows, and the smoothing and scales this launch wrote
-// (or the caller's smoothing), visible after the kernel's final block
-// barrier.  It writes the reference's exact code, clamp(lround(RN(RN(R / c) /
+// (0.812 -> 0.763 ms at 61,440 capsule heads, 0.863 -> 0.816 ms provider).
+// The late pass uses global memory only: the input rows, and the smoothing
+// and scales this launch wrote (or the caller's smoothing), visible after the
+// kernel's final block barrier.  It writes the reference's exact code, clamp(lround(RN(RN(R / c) /
 // b) * 127)), which equals the code already stored for every element that is
 // not ambiguous, so it rewrites whole chunks without testing them again.  A
 // thread with more than two flagged heads patches the extra ones at once
