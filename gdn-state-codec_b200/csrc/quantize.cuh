@@ -98,6 +98,7 @@ struct __align__(128) QuantizeGroupShared {
   uint32_t val_exact[kValues];         // IEEE path: maximum (bits)
   float colbuf[kKeys];                 // provider: one column for a sequential re-sum
   int col_flag[kKeys];
+  uint64_t owed[kQThreads][2];         // per thread: owed (head, mask) pairs, 0 = free
   uint64_t full;                       // landing buffer holds the next head (TMA bytes)
   uint64_t empty;                      // provider: every warp has copied the head
   int readers;                         // capsule: warps that have copied the current head
@@ -748,9 +749,12 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
     }
   }
   uint32_t parity = 0;
-  // Up to two owed (head, mask) pairs, each packed as mask << 32 | head (a
-  // head index above 32 bits, 256 TiB of state, is patched at once instead).
-  uint64_t owed0 = 0u, owed1 = 0u;
+  // Up to two owed (head, mask) pairs per thread, each packed as
+  // mask << 32 | head in shared memory (registers are at the kernel's limit;
+  // a head index above 32 bits, 256 TiB of state, is patched at once).
+  uint64_t* owed = gs.owed[gtid];
+  owed[0] = 0u;
+  owed[1] = 0u;
   while (head >= 0) {
     bool timed_out = !mbar_wait_bounded(&gs.full, parity, p.wait_limit_ns);
     CapsuleTile ct;
@@ -824,10 +828,10 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
     if (amb != 0u) {  // rare
       const uint64_t entry = static_cast<uint64_t>(amb) << 32 | static_cast<uint32_t>(head);
       const bool fits = (static_cast<uint64_t>(head) >> 32) == 0u;
-      if (fits && owed0 == 0u) {
-        owed0 = entry;
-      } else if (fits && owed1 == 0u) {
-        owed1 = entry;
+      if (fits && owed[0] == 0u) {
+        owed[0] = entry;
+      } else if (fits && owed[1] == 0u) {
+        owed[1] = entry;
       } else {
         pay_now<kProvider>(p, gs, head, warp, lane, amb);
       }
@@ -839,13 +843,13 @@ __global__ void __launch_bounds__(kQThreads, kQBlocksPerSm) quantize_kernel(Quan
   // last head's scales (the IEEE path writes them after its own barriers)
   // visible to the late pass.
   __syncthreads();
-  if (owed0 != 0u) {
-    pay_late<kProvider, kMode>(p, static_cast<uint32_t>(owed0), warp, lane,
-                               static_cast<uint32_t>(owed0 >> 32));
-  }
-  if (owed1 != 0u) {
-    pay_late<kProvider, kMode>(p, static_cast<uint32_t>(owed1), warp, lane,
-                               static_cast<uint32_t>(owed1 >> 32));
+#pragma unroll 1
+  for (int i = 0; i < 2; ++i) {
+    const uint64_t entry = owed[i];
+    if (entry != 0u) {
+      pay_late<kProvider, kMode>(p, static_cast<uint32_t>(entry), warp, lane,
+                                 static_cast<uint32_t>(entry >> 32));
+    }
   }
 }
 
