@@ -14,9 +14,11 @@
 //  * persistent 256-thread CTAs, two per SM.  Each walks its own sequence of
 //    heads with one 64 KiB shared-memory landing buffer filled by a single TMA
 //    bulk copy (cp.async.bulk + mbarrier, normal L2 policy); as soon as the
-//    CTA holds a head in registers the buffer takes its next head.  The two CTAs of an SM drift
-//    out of phase, so one's barriers and reductions overlap the other's
-//    arithmetic, and two heads are in flight per SM.
+//    CTA holds a head in registers the buffer takes its next head.  The two
+//    CTAs of an SM drift out of phase, so one's barriers and reductions
+//    overlap the other's arithmetic, and two heads are in flight per SM.
+//  * the rare elements next to a rounding boundary owe exact codes, written
+//    after the launch's last head (owed exact codes, below).
 //  * the smoothing sums run in double (tree order, with a proof-backed check
 //    that sends the rare order-sensitive rows to the reference's sequential
 //    order); every smoothed value s = R / c is computed correctly rounded from
