@@ -484,8 +484,8 @@ __device__ __forceinline__ bool quantize_capsule_head(const QuantizeParams& p,
     }
   }
   const float* head_state = p.state + static_cast<uint64_t>(head) * kElements;
-  // Rare: chunks near a rounding boundary owe exact codes; the kernel writes
-  // them after its last head (owe_codes), off this head's critical path.
+  // Rare: chunks near a rounding boundary owe exact codes; quantize_kernel
+  // writes them after its last head (pay_late), off this head's critical path.
   amb_out = amb_mask;
   if (any_slow) {  // rare and block-uniform: values outside the fast ranges
     slow_capsule_values(head_state, codes, p.scales + head * kValues, gs.key_c, gs.val_km,
@@ -620,8 +620,8 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
     amb_rows |= (amb ? 1u : 0u) << j;
   }
   const float* head_state = p.state + static_cast<uint64_t>(head) * kElements;
-  // Rare: rows near a rounding boundary owe exact codes; the kernel writes
-  // them after its last head (owe_codes), off this head's critical path.
+  // Rare: rows near a rounding boundary owe exact codes; quantize_kernel
+  // writes them after its last head (pay_late), off this head's critical path.
   amb_out = amb_rows;
   // IEEE path for rows outside the fast ranges (rare; all-zero rows included).
   if (slow_rows != 0u) {
@@ -636,14 +636,15 @@ __device__ __forceinline__ bool quantize_provider_head(const QuantizeParams& p,
 // near a rounding boundary records (head, mask) and writes the exact codes
 // after the launch's last head, so the IEEE divisions and the re-read of the
 // rows no longer hold its warp back from the next head's block barriers
-// (0.812 -> 0.763 ms at 61,440 capsule heads, 0.863 -> 0.816 ms provider).
-// The late pass uses global memory only: the input rows, and the smoothing
-// and scales this launch wrote (or the caller's smoothing), visible after the
-// kernel's final block barrier.  It writes the reference's exact code, clamp(lround(RN(RN(R / c) /
-// b) * 127)), which equals the code already stored for every element that is
-// not ambiguous, so it rewrites whole chunks without testing them again.  A
-// thread with more than two flagged heads patches the extra ones at once
-// from the head's shared arrays (patch_*_codes).
+// (0.812 -> 0.762 ms at 61,440 capsule heads, 0.863 -> 0.814 ms provider).
+// The late pass (pay_late) uses global memory only: the input rows, and the
+// smoothing and scales this launch wrote (or the caller's smoothing), visible
+// after the kernel's final block barrier.  It writes the reference's exact
+// code, clamp(lround(RN(RN(R / c) / b) * 127)), which equals the code already
+// stored for every element that is not ambiguous and is the IEEE path's own
+// formula, so it rewrites whole chunks without testing them again.  A thread
+// with more than two flagged heads patches the extra ones at once from the
+// head's shared arrays (pay_now, patch_*_codes).
 
 __device__ __noinline__ void late_capsule_codes(const float* head_state, const float* smoothing,
                                                 const float* scales, int8_t* codes, int row_base,
